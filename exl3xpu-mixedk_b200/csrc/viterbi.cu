@@ -1,0 +1,124 @@
+// viterbi.cu -- standalone tail-biting encoder over a batch of sequences.
+//
+// One 512-thread CTA encodes one sequence (it holds all of the SM's registers,
+// so one CTA per SM).  The host launches waves of at most `grid` CTAs
+// (grid <= SM count); CTA b of a wave uses backpointer slot b of the
+// workspace (256 * BP_ROW bytes), so a workspace of grid slots serves any
+// number of sequences.  A persistent per-CTA loop over sequences was
+// measured to cost register spills (loop-invariant addresses kept live
+// across the sequence loop); one sequence per CTA keeps the encoder
+// spill-free.
+#include "exl3b_internal.h"
+#include "viterbi.cuh"
+
+namespace exl3b {
+
+// One CTA of kVT threads writes the pre-paired decode words of every thread.
+template <int K>
+__global__ void __launch_bounds__(kVT)
+build_f2tab_kernel(const __half* __restrict__ lut16, uint4* __restrict__ tab) {
+    const int t = threadIdx.x;
+    __half2 f2[64];
+    vit_load_f<K>(f2, lut16, t);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        uint4 v;
+        v.x = *reinterpret_cast<uint32_t*>(&f2[4 * q + 0]);
+        v.y = *reinterpret_cast<uint32_t*>(&f2[4 * q + 1]);
+        v.z = *reinterpret_cast<uint32_t*>(&f2[4 * q + 2]);
+        v.w = *reinterpret_cast<uint32_t*>(&f2[4 * q + 3]);
+        tab[q * kVT + t] = v;
+    }
+}
+
+int build_f2tab(int K, const __half* lut16, uint4* tab, cudaStream_t stream) {
+    switch (K) {
+        case 2: build_f2tab_kernel<2><<<1, kVT, 0, stream>>>(lut16, tab); break;
+        case 3: build_f2tab_kernel<3><<<1, kVT, 0, stream>>>(lut16, tab); break;
+        case 4: build_f2tab_kernel<4><<<1, kVT, 0, stream>>>(lut16, tab); break;
+        case 5: build_f2tab_kernel<5><<<1, kVT, 0, stream>>>(lut16, tab); break;
+        case 6: build_f2tab_kernel<6><<<1, kVT, 0, stream>>>(lut16, tab); break;
+        case 7: build_f2tab_kernel<7><<<1, kVT, 0, stream>>>(lut16, tab); break;
+        default: set_error("K=%d outside 2..7", K); return RC_BAD_K;
+    }
+    return check_cuda(cudaGetLastError(), "build_f2tab launch") ? RC_DEVICE_ERROR : RC_OK;
+}
+
+template <int K>
+__global__ void __launch_bounds__(kVT, 1)
+tailbite_kernel(const float* __restrict__ X, int pivot, int margin,
+                int32_t* __restrict__ states, uint8_t* __restrict__ bp_ws,
+                const uint4* __restrict__ f2tab) {
+    extern __shared__ __align__(16) char smem[];
+    using SM = VitSmem<K>;
+    using G = Geo<K>;
+    const int t = threadIdx.x;
+    const int seq = blockIdx.x;
+    __half2 f2[64];
+    vit_load_f2tab(f2, f2tab, t);
+    float* xs = reinterpret_cast<float*>(smem + SM::OFF_X);
+    if (t < 64)
+        reinterpret_cast<float4*>(xs)[t] =
+            reinterpret_cast<const float4*>(X + (size_t)seq * kSteps)[t];
+    __syncthreads();
+    uint8_t* bp = bp_ws + (size_t)blockIdx.x * kSteps * G::BP_ROW;
+    vit_tailbite<K>(f2, smem, pivot, margin, bp, t);
+    if (t < kSteps)
+        states[(size_t)seq * kSteps + t] =
+            reinterpret_cast<const int32_t*>(smem + SM::OFF_ST)[t];
+}
+
+size_t bp_slot_bytes(int K) {
+    switch (K) {
+        case 2: return (size_t)kSteps * Geo<2>::BP_ROW;
+        case 3: return (size_t)kSteps * Geo<3>::BP_ROW;
+        case 4: return (size_t)kSteps * Geo<4>::BP_ROW;
+        case 5: return (size_t)kSteps * Geo<5>::BP_ROW;
+        case 6: return (size_t)kSteps * Geo<6>::BP_ROW;
+        case 7: return (size_t)kSteps * Geo<7>::BP_ROW;
+    }
+    return 0;
+}
+
+template <int K>
+static int launch_k(const float* dX, int nseq, int pivot, int margin,
+                    int32_t* dStates, uint8_t* ws, int grid,
+                    const uint4* f2tab, cudaStream_t stream) {
+    const int smem = VitSmem<K>::BYTES;
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev]) {
+        if (check_cuda(cudaFuncSetAttribute(tailbite_kernel<K>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                       "cudaFuncSetAttribute(tailbite)"))
+            return RC_DEVICE_ERROR;
+        attr_set[dev] = true;
+    }
+    for (int s0 = 0; s0 < nseq; s0 += grid) {
+        const int n = nseq - s0 < grid ? nseq - s0 : grid;
+        tailbite_kernel<K><<<n, kVT, smem, stream>>>(
+            dX + (size_t)s0 * kSteps, pivot, margin, dStates + (size_t)s0 * kSteps,
+            ws, f2tab);
+        if (check_cuda(cudaGetLastError(), "tailbite_kernel launch"))
+            return RC_DEVICE_ERROR;
+    }
+    return RC_OK;
+}
+
+int launch_tailbite(const float* dX, int nseq, int K, int pivot, int margin,
+                    int32_t* dStates, uint8_t* ws, int grid,
+                    const uint4* f2tab, cudaStream_t stream) {
+    switch (K) {
+        case 2: return launch_k<2>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
+        case 3: return launch_k<3>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
+        case 4: return launch_k<4>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
+        case 5: return launch_k<5>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
+        case 6: return launch_k<6>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
+        case 7: return launch_k<7>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
+    }
+    set_error("K=%d outside 2..7", K);
+    return RC_BAD_K;
+}
+
+}  // namespace exl3b

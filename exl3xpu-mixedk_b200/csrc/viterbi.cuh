@@ -1,0 +1,375 @@
+// viterbi.cuh -- tail-biting trellis Viterbi for one 16x16 tile per CTA.
+//
+// Algorithm (reference: quantize/quantize.py:218-354, viterbi() and
+// quantize_seq_tailbite(), emit_mode "sq"): 256-step shift-register trellis,
+// 16-bit state s, K bits enter per step, decode value f(s) = lut[s].
+//   cost_0(s)  = (f(s) - x_0)^2                    (+ 0/inf boundary mask)
+//   best_i(j)  = min_w cost_{i-1}(j + w*2^(16-K))   first index on ties
+//   cost_i(s)  = (f(s) - x_i)^2 + best_i(s >> K)
+// Two passes: pass 1 on the sequence rolled by `pivot` with a free boundary
+// (optionally only pivot+margin steps), giving the wrap bits; pass 2 pinned to
+// them at both ends.
+//
+// B200 design:
+//  * The 2^16-entry cost table is never stored.  Only best_i (2^(16-K) fp32)
+//    lives in shared memory, double-buffered; cost_i(s) is recomputed inside
+//    the min of the next step.  fp32 operations and their order are the
+//    reference's, so the result is bit-identical.
+//  * The trellis splits into 2^(16-2K) butterflies: inputs best_i[m + w*P]
+//    (w < 2^K, P = 2^(16-2K)) feed outputs best_{i+1}[m*2^K + v].  Each of the
+//    512 threads owns 128 fixed states (whole butterflies for K <= 3, a slice of
+//    one butterfly for K >= 4) and holds their decode values in 64 packed-fp16
+//    registers for the whole kernel (EXL3 decode values are exact in fp16), so
+//    one add-compare-select is: unpack, fsub, fmul, fadd, compare, 2 selects --
+//    no shared-memory gather on the inner loop.
+//  * Backpointers: each thread packs its outputs' K-bit argmins into one
+//    8/16/32/64-bit word per step and stores it coalesced to global scratch
+//    (row of 512 words per step).  Traceback runs on device: the CTA stages
+//    chunks of rows into shared memory, one thread follows the path.
+#pragma once
+#include "exl3b_common.cuh"
+
+namespace exl3b {
+
+constexpr int kVT = 512;                 // threads per tile CTA
+constexpr int kTbBytes = 64 * 1024;      // traceback staging buffer
+
+template <int K>
+struct Geo {
+    static_assert(K >= 2 && K <= 7, "K must be 2..7");
+    static constexpr int NC = 1 << K;                 // predecessors per state
+    static constexpr int SPRE = 1 << (16 - K);        // best-array size
+    static constexpr int LOGP = 16 - 2 * K;
+    static constexpr int P = 1 << LOGP;               // butterflies
+    static constexpr bool WHOLE = P >= kVT;           // K <= 3
+    static constexpr int NB = WHOLE ? P / kVT : 1;    // butterflies per thread
+    static constexpr int TPB = WHOLE ? 1 : kVT / P;   // threads per butterfly
+    static constexpr int NJ = WHOLE ? NC : NC / TPB;  // outputs per butterfly per thread
+    static constexpr int NOUT = NB * NJ;              // outputs per thread
+    static constexpr int NSTATE = NOUT * NC;          // states per thread (128)
+    static_assert(NSTATE == 128, "each thread owns 128 states");
+    static constexpr int BPE = (K <= 2) ? 2 : (K <= 4 ? 4 : 8);  // bits / backpointer
+    static constexpr int BPTB = NOUT * BPE / 8;       // backpointer bytes / thread / step
+    static constexpr int BP_ROW = kVT * BPTB;         // backpointer bytes per step
+    static constexpr int TB_ROWS = kTbBytes / BP_ROW; // rows per traceback chunk
+    static constexpr bool TRANSPOSED = K >= 5;        // best-array smem layout
+    static constexpr int NCH = (NJ >= 4) ? 1 : 4 / NJ;  // partial min chains
+
+    // output index j of thread t's e-th output
+    static __device__ __forceinline__ int out_j(int t, int e) {
+        if (WHOLE) return (t + kVT * (e / NC)) * NC + (e % NC);
+        return t * NJ + e;
+    }
+    // butterfly of thread t for its b-th butterfly
+    static __device__ __forceinline__ int bfly(int t, int b) {
+        return WHOLE ? t + kVT * b : t / TPB;
+    }
+    // shared-memory address of best[idx].  Transposed for K >= 5 so that a
+    // butterfly's 2^K inputs are contiguous (vector loads).
+    static __device__ __forceinline__ int baddr(int idx) {
+        if (TRANSPOSED) return (idx & (P - 1)) * NC + (idx >> LOGP);
+        return idx;
+    }
+    // backpointer of output j inside one staged row
+    static __device__ __forceinline__ int bp_read(const uint8_t* row, int j) {
+        int tt, e;
+        if (WHOLE) {
+            const int m = j >> K;
+            tt = m & (kVT - 1);
+            e = (m / kVT) * NC + (j & (NC - 1));
+        } else {
+            tt = j / NJ;
+            e = j % NJ;
+        }
+        const int bit = e * BPE;
+        const int byte = row[tt * BPTB + (bit >> 3)];
+        return (byte >> (bit & 7)) & ((1 << BPE) - 1);
+    }
+};
+
+// Shared-memory layout of a tile CTA (dynamic shared memory).
+template <int K>
+struct VitSmem {
+    static constexpr int B_BYTES = Geo<K>::SPRE * 4;
+    static constexpr int OFF_B0 = 0;
+    static constexpr int OFF_B1 = B_BYTES;
+    static constexpr int OFF_X = 2 * B_BYTES;          // 256 fp32 targets
+    static constexpr int OFF_ST = OFF_X + 1024;        // 256 int32 states
+    static constexpr int OFF_RED = OFF_ST + 1024;      // reduction scratch
+    static constexpr int OFF_TB = OFF_RED + 256;       // traceback rows
+    static constexpr int OFF_EXTRA = OFF_TB + kTbBytes; // caller-owned tail
+    static constexpr int BYTES = OFF_EXTRA;
+};
+
+// Load this thread's 128 decode values (fp16-exact) into packed registers.
+template <int K>
+__device__ __forceinline__ void vit_load_f(__half2 (&f2)[64],
+                                           const __half* __restrict__ lut16,
+                                           int t) {
+    using G = Geo<K>;
+#pragma unroll
+    for (int e = 0; e < G::NOUT; ++e) {
+        const int j = G::out_j(t, e);
+#pragma unroll
+        for (int w = 0; w < G::NC; w += 2) {
+            const __half a = lut16[j + w * G::SPRE];
+            const __half b = lut16[j + (w + 1) * G::SPRE];
+            f2[(e * G::NC + w) >> 1] = __halves2half2(a, b);
+        }
+    }
+}
+
+// Same 64 words from a pre-paired table laid out [16][kVT] uint4 (word r2 of
+// thread t in component r2 % 4 of entry (r2 / 4) * kVT + t): 16 coalesced
+// 16-byte loads instead of 128 scattered half loads.
+__device__ __forceinline__ void vit_load_f2tab(__half2 (&f2)[64],
+                                               const uint4* __restrict__ tab,
+                                               int t) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        uint4 v = tab[q * kVT + t];
+        f2[4 * q + 0] = *reinterpret_cast<__half2*>(&v.x);
+        f2[4 * q + 1] = *reinterpret_cast<__half2*>(&v.y);
+        f2[4 * q + 2] = *reinterpret_cast<__half2*>(&v.z);
+        f2[4 * q + 3] = *reinterpret_cast<__half2*>(&v.w);
+    }
+}
+
+// d = fl(f - x) with f the low (HI=false) or high half of a packed pair.  The
+// unpack and the subtraction sit in one asm block that consumes x, so the
+// compiler cannot hoist 128 unpacked decode values out of the step loop
+// (which would need 128 extra registers).
+template <bool HI>
+__device__ __forceinline__ float sub_f16(__half2 h2, float x) {
+    const uint32_t r = *reinterpret_cast<const uint32_t*>(&h2);
+    float d;
+    if (HI)
+        asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 f;\n\t"
+            "mov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 f, hi;\n\t"
+            "sub.rn.f32 %0, f, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
+    else
+        asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 f;\n\t"
+            "mov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 f, lo;\n\t"
+            "sub.rn.f32 %0, f, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
+    return d;
+}
+
+template <int K>
+__device__ __forceinline__ float vit_d(const __half2 (&f2)[64], int r, float x) {
+    return (r & 1) ? sub_f16<true>(f2[r >> 1], x) : sub_f16<false>(f2[r >> 1], x);
+}
+
+// Compare-and-update of one add-compare-select: if c < best then best = c and
+// the bit field [pos, pos+len) of `idx` becomes w.  Strict < keeps the first
+// (lowest) w on ties, like torch.min.  Predicated so that, with w / pos / len
+// compile-time constants, it issues as setp + 2 predicated ops.
+__device__ __forceinline__ void acs_update(float& best, uint32_t& idx, float c,
+                                           uint32_t clear_mask, uint32_t setv) {
+    asm("{\n\t.reg .pred p;\n\t"
+        "setp.lt.f32 p, %2, %0;\n\t"
+        "@p mov.f32 %0, %2;\n\t"
+        "@p and.b32 %1, %1, %3;\n\t"
+        "@p or.b32 %1, %1, %4;\n\t}"
+        : "+f"(best), "+r"(idx)
+        : "f"(c), "r"(clear_mask), "r"(setv));
+}
+
+// One trellis step: best_{i+1} = min-plus over this thread's states using
+// best_i (Bc) and target x; writes best_{i+1} (Bn), returns packed argmins
+// (output e's argmin w in bits [e*BPE, e*BPE + BPE)).
+template <int K>
+__device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
+                                             const float* __restrict__ Bc,
+                                             float* __restrict__ Bn, int t) {
+    using G = Geo<K>;
+    constexpr int NCH = G::NCH;
+    constexpr int BPE = G::BPE;
+    constexpr uint32_t FM = (1u << BPE) - 1u;
+    uint64_t bits = 0;
+#pragma unroll
+    for (int b = 0; b < G::NB; ++b) {
+        const int m = G::bfly(t, b);
+        float best[G::NJ][NCH];
+        uint32_t pk[NCH];             // packed argmins of this butterfly slice
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) pk[ch] = 0u;
+#pragma unroll
+        for (int w4 = 0; w4 < G::NC; w4 += 4) {
+            float bin[4];
+            if (G::TRANSPOSED) {
+                const float4 q = *reinterpret_cast<const float4*>(&Bc[m * G::NC + w4]);
+                bin[0] = q.x; bin[1] = q.y; bin[2] = q.z; bin[3] = q.w;
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) bin[q] = Bc[m + (w4 + q) * G::P];
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int w = w4 + q;
+                const int ch = w % NCH;
+#pragma unroll
+                for (int u = 0; u < G::NJ; ++u) {
+                    const float d = vit_d<K>(f2, (b * G::NJ + u) * G::NC + w, x);
+                    const float c = __fadd_rn(__fmul_rn(d, d), bin[q]);
+                    const int pos = u * BPE;
+                    if (w < NCH) {
+                        best[u][ch] = c;
+                        if (w) pk[ch] |= (uint32_t)w << pos;
+                    } else {
+                        acs_update(best[u][ch], pk[ch], c, ~(FM << pos),
+                                   (uint32_t)w << pos);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < G::NJ; ++u) {
+            const int pos = u * BPE;
+            float bv = best[u][0];
+            uint32_t bx = (pk[0] >> pos) & FM;
+#pragma unroll
+            for (int ch = 1; ch < NCH; ++ch) {   // (value, index) lexicographic
+                const uint32_t ix = (pk[ch] >> pos) & FM;
+                const bool take = best[u][ch] < bv || (best[u][ch] == bv && ix < bx);
+                bv = take ? best[u][ch] : bv;
+                bx = take ? ix : bx;
+            }
+            const int e = b * G::NJ + u;
+            Bn[G::baddr(G::out_j(t, e))] = bv;
+            if (NCH == 1) {
+                if (u == 0) bits |= static_cast<uint64_t>(pk[0]) << (b * G::NJ * BPE);
+            } else {
+                bits |= static_cast<uint64_t>(bx) << (e * BPE);
+            }
+        }
+    }
+    return bits;
+}
+
+template <int K>
+__device__ __forceinline__ void vit_store_bits(uint8_t* __restrict__ row,
+                                               uint64_t bits, int t) {
+    using G = Geo<K>;
+    if (G::BPTB == 8) reinterpret_cast<uint64_t*>(row)[t] = bits;
+    else if (G::BPTB == 4) reinterpret_cast<uint32_t*>(row)[t] = (uint32_t)bits;
+    else if (G::BPTB == 2) reinterpret_cast<uint16_t*>(row)[t] = (uint16_t)bits;
+    else row[t] = (uint8_t)bits;
+}
+
+__device__ __forceinline__ void lex_min(float& c, int& s, float oc, int os) {
+    const bool take = oc < c || (oc == c && os < s);
+    c = take ? oc : c;
+    s = take ? os : s;
+}
+
+// One Viterbi pass over `nsteps` targets xs[(i - rol) & 255].
+//   overlap < 0 : free boundary;  >= 0 : s_0>>K and s_last mod 2^(16-K) pinned.
+//   stop        : traceback ends at step `stop` (state returned).
+//   st          : if non-null, receives states[0..nsteps) (pass 2).
+// bp: this CTA's global backpointer rows [256][BP_ROW].  All threads return
+// the state at step `stop`.
+template <int K>
+__device__ __forceinline__ int vit_pass(const __half2 (&f2)[64], char* smem, int rol,
+                        int nsteps, int overlap, int stop, int32_t* st,
+                        uint8_t* __restrict__ bp, int t) {
+    using G = Geo<K>;
+    using SM = VitSmem<K>;
+    float* Bc = reinterpret_cast<float*>(smem + SM::OFF_B0);
+    float* Bn = reinterpret_cast<float*>(smem + SM::OFF_B1);
+    const float* xs = reinterpret_cast<const float*>(smem + SM::OFF_X);
+    float* redc = reinterpret_cast<float*>(smem + SM::OFF_RED);
+    int* reds = reinterpret_cast<int*>(smem + SM::OFF_RED + 64);
+    int* bcast = reinterpret_cast<int*>(smem + SM::OFF_RED + 128);
+    const float INF = __int_as_float(0x7f800000);
+
+    // best_0: 0 (free) or 0 at `overlap`, +inf elsewhere -> cost_0 = E_0 + mask
+    for (int idx = t; idx < G::SPRE; idx += kVT)
+        Bc[G::baddr(idx)] = (overlap < 0 || idx == overlap) ? 0.0f : INF;
+    __syncthreads();
+
+    for (int i = 0; i < nsteps - 1; ++i) {
+        const float x = xs[(i - rol) & 255];
+        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t);
+        if (i + 1 > stop) vit_store_bits<K>(bp + (size_t)(i + 1) * G::BP_ROW, bits, t);
+        float* tmp = Bc; Bc = Bn; Bn = tmp;
+        __syncthreads();
+    }
+
+    // Final argmin over cost_{n-1}(s), lowest s on ties (torch.argmin).  One
+    // more step gives best_n[j] = min_w cost_{n-1}(j + w*2^(16-K)) with the
+    // first w attaining it, i.e. the lowest state of group j at that value;
+    // the lexicographic (value, state) minimum over all groups is the global
+    // first-index argmin.  Pass 2's end mask (s mod 2^(16-K) == overlap, +inf
+    // elsewhere) keeps only group j == overlap.
+    {
+        const float x = xs[(nsteps - 1 - rol) & 255];
+        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t);
+        float bc = INF;
+        int bs = 0x7fffffff;
+#pragma unroll
+        for (int e = 0; e < G::NOUT; ++e) {
+            const int j = G::out_j(t, e);
+            float v = Bn[G::baddr(j)];
+            if (overlap >= 0 && j != overlap) v = INF;
+            const int w = (int)((bits >> (e * G::BPE)) & ((1u << G::BPE) - 1u));
+            lex_min(bc, bs, v, j + (w << (16 - K)));
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float oc = __shfl_xor_sync(0xffffffffu, bc, off);
+            const int os = __shfl_xor_sync(0xffffffffu, bs, off);
+            lex_min(bc, bs, oc, os);
+        }
+        if ((t & 31) == 0) { redc[t >> 5] = bc; reds[t >> 5] = bs; }
+        __syncthreads();
+    }
+
+    // traceback (thread 0), backpointer rows staged through shared memory
+    int s = 0;
+    if (t == 0) {
+        float bc = redc[0];
+        s = reds[0];
+        for (int wv = 1; wv < kVT / 32; ++wv) lex_min(bc, s, redc[wv], reds[wv]);
+        if (st) st[nsteps - 1] = s;
+    }
+    uint8_t* tb = reinterpret_cast<uint8_t*>(smem + SM::OFF_TB);
+    int hi = nsteps - 1;
+    while (hi > stop) {
+        const int lo = max(stop + 1, hi - G::TB_ROWS + 1);
+        const int n16 = (hi - lo + 1) * (G::BP_ROW / 16);
+        const uint4* src = reinterpret_cast<const uint4*>(bp + (size_t)lo * G::BP_ROW);
+        uint4* dst = reinterpret_cast<uint4*>(tb);
+        for (int q = t; q < n16; q += kVT) dst[q] = src[q];
+        __syncthreads();
+        if (t == 0) {
+            for (int i = hi; i >= lo; --i) {
+                const int j = s >> K;
+                const int w = G::bp_read(tb + (size_t)(i - lo) * G::BP_ROW, j);
+                s = j + (w << (16 - K));
+                if (st) st[i - 1] = s;
+            }
+        }
+        __syncthreads();
+        hi = lo - 1;
+    }
+    if (t == 0) *bcast = s;
+    __syncthreads();
+    const int out = *bcast;
+    __syncthreads();
+    return out;
+}
+
+// Full tail-biting encode of the tile whose 256 targets sit in smem OFF_X.
+// Writes the 256 pass-2 states to smem OFF_ST.
+template <int K>
+__device__ __forceinline__ void vit_tailbite(const __half2 (&f2)[64], char* smem,
+                                             int pivot, int margin,
+                                             uint8_t* __restrict__ bp, int t) {
+    using SM = VitSmem<K>;
+    int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST);
+    const int n1 = (margin > 0 && pivot + margin < kSteps) ? pivot + margin : kSteps;
+    const int sp = vit_pass<K>(f2, smem, pivot, n1, -1, pivot, nullptr, bp, t);
+    vit_pass<K>(f2, smem, 0, kSteps, sp >> K, 0, st, bp, t);
+}
+
+}  // namespace exl3b

@@ -1,0 +1,108 @@
+"""GPU parity of the CUDA tail-biting encoder against the reference's golden
+states and the CPU oracle.  The bar is bit-exact states: the kernel keeps the
+reference's fp32 operation order (fl(fl(f - x)^2) + best, first index on
+ties), so any difference is a bug."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+NTHREADS = max(1, min(32, os.cpu_count() or 1))
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from exl3b import ops as _ops
+    return _ops
+
+
+def _run(ops, X, K, pivot, margin):
+    st = ops.tailbite(torch.from_numpy(X).cuda(), K, pivot=pivot, margin=margin)
+    torch.cuda.synchronize()
+    return st.cpu().numpy()
+
+
+@pytest.mark.parametrize("K", range(2, 8))
+def test_golden_states(ops, K):
+    """Every reference-generated case (Gaussian, tie-heavy, wide targets;
+    six pivot/margin combinations)."""
+    g = golden("viterbi")
+    n = 0
+    for key in g.files:
+        if not key.startswith("st_") or f"_K{K}_" not in key:
+            continue
+        _, tag, _, p, m = key.split("_")
+        st = _run(ops, g[f"X_{tag}"], K, int(p[1:]), int(m[1:]))
+        assert np.array_equal(st.astype(np.uint16), g[key]), key
+        n += 1
+    assert n >= 8
+
+
+@pytest.mark.parametrize("K,nseq,pivot,margin", [
+    (4, 300, 128, 0),      # more sequences than SMs: several waves
+    (4, 160, 0, 16),       # quantize() defaults at seed 0
+    (2, 48, 77, 16), (3, 48, 255, 0), (5, 48, 3, 40),
+    (6, 48, 128, 0), (7, 48, 200, 100),
+])
+def test_random_vs_oracle(ops, oracle, mul1_lut, K, nseq, pivot, margin):
+    rng = np.random.default_rng(1000 + K * 7 + pivot)
+    X = rng.standard_normal((nseq, 256)).astype(np.float32)
+    X[: nseq // 4] *= 0.05                       # small-magnitude tiles
+    X[nseq // 4: nseq // 2] = np.round(X[nseq // 4: nseq // 2] * 4) / 4  # coarse grid: ties
+    st = _run(ops, X, K, pivot, margin)
+    ref = oracle.tailbite(X, mul1_lut, K, pivot=pivot, margin=margin, nthreads=NTHREADS)
+    bad = np.nonzero((st != ref).any(1))[0]
+    assert bad.size == 0, f"{bad.size} sequences differ, first {bad[:5]}"
+    # tail-biting consistency (test_quantize.py:141-152)
+    assert np.all((st[:, 0] >> K) == (st[:, -1] & ((1 << (16 - K)) - 1)))
+
+
+def test_other_codes(ops, oracle):
+    """3INST / MCG tables go through the same encoder."""
+    rng = np.random.default_rng(7)
+    X = rng.standard_normal((12, 256)).astype(np.float32)
+    for code in ("exl3_3inst", "exl3_mcg"):
+        st = ops.tailbite(torch.from_numpy(X).cuda(), 4, pivot=10, margin=0, code=code)
+        ref = oracle.tailbite(X, oracle.code_lut(code), 4, pivot=10, margin=0,
+                              nthreads=NTHREADS)
+        assert np.array_equal(st.cpu().numpy(), ref), code
+
+
+def test_xtq_vit_run_dropin(oracle, mul1_lut):
+    """The reference's ctypes entry points (viterbi_esimd.cpp:935-1005):
+    same signature, host buffers, mul1 at K=4, same return codes."""
+    from exl3b import native
+    L = native.lib()
+    assert L.xtq_vit_init() == 0
+    rng = np.random.default_rng(5)
+    X = np.ascontiguousarray(rng.standard_normal((20, 256)).astype(np.float32))
+    out = np.zeros((20, 256), dtype=np.int32)
+    P = ctypes.c_void_p
+    rc = L.xtq_vit_run(X.ctypes.data_as(P), 20, b"mul1p", 16, 40, out.ctypes.data_as(P))
+    assert rc == 0, native.last_error()
+    ref = oracle.tailbite(X, mul1_lut, 4, pivot=40, margin=16, nthreads=NTHREADS)
+    assert np.array_equal(out, ref)
+    assert L.xtq_vit_run(X.ctypes.data_as(P), 0, b"mul1p", 0, 0, out.ctypes.data_as(P)) == 6
+    assert L.xtq_vit_run(X.ctypes.data_as(P), 20, b"ih2x2", 0, 0, out.ctypes.data_as(P)) == 7
+    assert L.xtq_vit_run(X.ctypes.data_as(P), 5000, b"mul1p", 0, 0, out.ctypes.data_as(P)) == 6
+
+
+def test_workspace_validation(ops):
+    from exl3b import native
+    L = native.lib()
+    X = torch.zeros(4, 256, device="cuda")
+    S = torch.zeros(4, 256, dtype=torch.int32, device="cuda")
+    need = L.exl3b_tailbite_workspace_bytes(4, 4)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    rc = L.exl3b_tailbite(X.data_ptr(), 4, 4, 0, 0, 0, S.data_ptr(), ws.data_ptr(),
+                          need - 1, None)
+    assert rc == 11
+    rc = L.exl3b_tailbite(X.data_ptr(), 4, 4, 0, 0, 0, S.data_ptr(), None, 0, None)
+    assert rc == 0, native.last_error()
+    torch.cuda.synchronize()
