@@ -1,5 +1,6 @@
 // exl3b_internal.h -- host-side declarations shared by the .cu files.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -44,5 +45,84 @@ int build_f2tab(int K, const __half* lut16, uint4* tab, cudaStream_t stream);
 int launch_tailbite(const float* dX, int nseq, int K, int pivot, int margin,
                     int32_t* dStates, uint8_t* ws, int grid,
                     const uint4* f2tab, cudaStream_t stream);
+
+// ------------------------------------------------------------ incoherence
+struct HadParams {
+    const void* X;      // input matrix
+    int in_dtype;       // 0 fp32, 1 bf16, 2 fp16
+    int ldx;            // input row stride (elements)
+    bool trans_in;      // block element (r, c) = X[c][r] instead of X[r][c]
+    float* Y;           // output fp32
+    int ldy;
+    bool trans_out;     // write Y[c][r]
+    int rows, cols;     // logical matrix (after trans_in), multiples of 128
+    float pre_scale;    // scalar multiply on load
+    const float* pre_scale_dev;  // device scalar multiply on load (nullable)
+    const float* pre_r; // per-row multiplier on load (nullable)
+    const float* pre_c; // per-col multiplier on load (nullable)
+    const float* mid_r; // per-row multiplier between the transforms
+    const float* post_c;// per-col multiplier after both transforms
+    double* sumsq;      // per-block sum of squares of Y (nullable), [nblocks]
+    const float* pre_r_div;  // per-row divisor on load (nullable)
+    const float* pre_c_div;  // per-col divisor on load (nullable)
+    bool skip_left;     // no transform along rows (r)
+    bool skip_right;    // no transform along cols (c)
+    double* row_sumsq;  // per-row partial sums of squares [rows][cols/128]
+};
+
+int launch_had2(const HadParams& p, cudaStream_t stream);
+int launch_transpose_scale(bool inv, const float* X, int rows_x, int cols_x,
+                           const float* rmag, const float* cmag, const float* s,
+                           float* Y, double* sumsq, cudaStream_t stream);
+int launch_rms_scale(const double* partials, int nparts, double count, float lut_rms,
+                     double* tmp1, float* scale, cudaStream_t stream);
+int launch_div_scalar(const float* x, const float* s, float* y, size_t n, cudaStream_t stream);
+int launch_damp(float* G, int k, float percdamp, cudaStream_t stream);
+int launch_count_nonfinite(const float* G, size_t n, int* cnt, cudaStream_t stream);
+int launch_damp_f64(double* G, int k, double extra, cudaStream_t stream);
+int launch_row_rms(const void* X, int dtype, int rows, int cols, float* rms, cudaStream_t stream);
+int launch_chan_out(float* r_out, const float* sv, int n, float* div_c, float* store_c,
+                    cudaStream_t stream);
+int launch_chan_in(const double* row_parts, int k, int nparts, const float* su, float* r_in,
+                   float* div_r, cudaStream_t stream);
+int launch_chan_store(const float* su, const float* r_in, const float* wscale,
+                      const float* sv, const float* store_c, int k, int n,
+                      __half* suh, __half* svh, cudaStream_t stream);
+int launch_f32_to_f64(const float* a, double* b, size_t n, cudaStream_t stream);
+
+// ------------------------------------------------------------ factorisation
+template <typename T>
+int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream_t stream);
+int u_to_gram_f64(const float* U, int n, double* Ud, double* Ui, double* G, cudaStream_t stream);
+int launch_gemm_tn_acc_f32(int M, int N, int K, const float* A_T, int lda,
+                           const float* B, int ldb, float* C, int ldc, cudaStream_t stream);
+
+// ------------------------------------------------------------ LDLQ sweep
+struct SweepArgs {
+    const float* Wq;
+    const float* Lfac;
+    int k, n;
+    int nseg;
+    const int* seg_c0;       // [nseg + 1] column tiles
+    const int* seg_K;
+    int16_t* const* seg_trellis;
+    int pivot, margin, buf_cols;
+    float* hatW;
+    float* E;
+    float* prod;
+    int32_t* states;
+    float* xout;
+    uint8_t* bp_ws;
+    size_t bp_slot;
+    int wave;                // CTAs per wave (= bp slots)
+    const uint4* const* f2tab;  // [8] per K
+    const float* lut32;
+    int block_hi, block_lo;  // sweep blocks [block_lo, block_hi)
+};
+int ldlq_sweep(const SweepArgs& a, cudaStream_t stream);
+int launch_pack(const int32_t* st, int nt, int K, int16_t* out, cudaStream_t stream);
+int launch_unpack(const int16_t* tr, int nt, int K, int32_t* st, cudaStream_t stream);
+int launch_decode(const int16_t* tr, int tk, int tn, int K, const float* lut, float* W,
+                  cudaStream_t stream);
 
 }  // namespace exl3b

@@ -39,6 +39,28 @@ SIGNATURES = {
     "exl3b_tailbite": (I, [P, I, I, I, I, I, P, P, SZ, P]),
     "xtq_vit_init": (I, []),
     "xtq_vit_run": (I, [P, I, ctypes.c_char_p, I, I, P]),
+    "exl3b_incoherence_fwd": (I, [P, I, I, I, P, P, P, P, P]),
+    "exl3b_incoherence_inv": (I, [P, I, I, P, P, P, P, P]),
+    "exl3b_rotate_hessian": (I, [P, I, P, P, P]),
+    "exl3b_channel_scale_workspace_bytes": (SZ, [I, I]),
+    "exl3b_channel_scale_fwd": (I, [P, I, I, I, P, P, P, P, P, P, P, P, SZ, P]),
+    "exl3b_channel_scale_store": (I, [P, P, P, P, P, I, I, P, P, P]),
+    "exl3b_damp_hessian": (I, [P, I, F, P, P]),
+    "exl3b_convert_f32_f64": (I, [P, P, SZ, P]),
+    "exl3b_damp_hessian_f64": (I, [P, I, D, P]),
+    "exl3b_transpose_scale": (I, [I, P, I, I, P, P, P, P, P, P]),
+    "exl3b_rms_scale": (I, [P, I, D, F, P, P, P]),
+    "exl3b_div_scalar": (I, [P, P, P, SZ, P]),
+    "exl3b_block_ldl_workspace_bytes": (SZ, [I, I]),
+    "exl3b_block_ldl": (I, [P, I, I, P, P, P, SZ, P]),
+    "exl3b_u_to_gram_workspace_bytes": (SZ, [I]),
+    "exl3b_u_to_gram": (I, [P, I, P, P, SZ, P]),
+    "exl3b_ldlq_workspace_bytes": (SZ, [I, I, I, I]),
+    "exl3b_ldlq_sweep": (I, [P, P, I, I, I, P, P, P, I, I, I, I, P, P, P, I, I,
+                             P, SZ, P]),
+    "exl3b_pack_states": (I, [P, I, I, P, P]),
+    "exl3b_unpack_states": (I, [P, I, I, P, P]),
+    "exl3b_decode_trellis": (I, [P, I, I, I, I, P, P]),
 }
 
 

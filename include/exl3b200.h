@@ -84,6 +84,136 @@ int xtq_vit_init(void);
 int xtq_vit_run(const float* X, int nseq, const char* code, int margin,
                 int pivot, int32_t* out);
 
+
+/* ===================================================================
+ * Quantizer pipeline (quantize/quantize.py:749-966).  Device pointers,
+ * asynchronous on `stream` unless stated.  Matrices are row-major;
+ * "[k][n]" is the reference's inner orientation (k = in, n = out).
+ * =================================================================== */
+
+/* Incoherence, forward (to_inner, quantize.py:149-155):
+ *   Wi[k][n] = B_128 . diag(row_mul) . W^T . diag(col_mul) . B_128
+ * W [m_out][k_in] of dtype 0 = fp32, 1 = bf16, 2 = fp16; row_mul [k_in] and
+ * col_mul [m_out] multipliers (1/suh, 1/svh) or NULL; both dims multiples of
+ * 128.  sumsq_parts (nullable, [(k/128)*(n/128)] fp64) receives per-block
+ * sums of squares of Wi (deterministic rms). */
+int exl3b_incoherence_fwd(const void* dW, int dtype, int m_out, int k_in,
+                          const float* d_row_mul, const float* d_col_mul,
+                          float* dWi, double* d_sumsq_parts, void* stream);
+
+/* Incoherence, inverse (from_inner, quantize.py:158-164), output transposed:
+ *   W[n][k] = ((B . (s * Wi) ) * su[:,None] . B * sv[None,:])^T
+ * with s = *d_pre_scale (device scalar, nullable = 1). */
+int exl3b_incoherence_inv(const float* dWi, int k, int n, const float* d_pre_scale,
+                          const float* d_su, const float* d_sv, float* dW,
+                          void* stream);
+
+/* EXL3 per-channel magnitude folds (quantize_linear channel_scales=True,
+ * quantize.py:785-800; prepare_incoherence :1025-1041):
+ *   sv_mag = rms_in(W) / mean(rms_in(W)), 0.1 where ~0 (sv_store: 0 there)
+ *   w = had_right(W^T / (sv * sv_mag));  su_mag = rms_out(w) (0.1 where ~0)
+ *   Wi[k][n] = had_left(w / (su * su_mag))
+ * su/sv are the sign vectors (fp32 +-1).  Outputs su_mag [k], sv_mag [n],
+ * sv_store [n]; sumsq_parts as in exl3b_incoherence_fwd. */
+size_t exl3b_channel_scale_workspace_bytes(int m_out, int k_in);
+int exl3b_channel_scale_fwd(const void* dW, int dtype, int m_out, int k_in,
+                            const float* d_su, const float* d_sv, float* dWi,
+                            float* d_su_mag, float* d_sv_mag, float* d_sv_store,
+                            double* d_sumsq_parts, void* ws, size_t ws_bytes,
+                            void* stream);
+
+/* Stored EXL3 fields (quantize.py:857-858): suh = fp16(su * su_mag * Wscale)
+ * (d_wscale nullable = 1), svh = fp16(sv * sv_store). */
+int exl3b_channel_scale_store(const float* d_su, const float* d_su_mag,
+                              const float* d_wscale, const float* d_sv,
+                              const float* d_sv_store, int k, int n,
+                              void* d_suh_f16, void* d_svh_f16, void* stream);
+
+/* Hessian rotation (rotate_hessian, quantize.py:167-176):
+ *   G = B . diag(su) . H . diag(su) . B,  H, G fp32 [k][k]. */
+int exl3b_rotate_hessian(const float* dH, int k, const float* d_su, float* dG,
+                         void* stream);
+
+/* Damping (quantize.py:810-814): dead diagonal entries -> 1, then
+ * diag += percdamp * mean(diag).  d_nonfinite (nullable) receives the count
+ * of non-finite entries of the damped G. */
+int exl3b_damp_hessian(float* dG, int k, float percdamp, int* d_nonfinite,
+                       void* stream);
+
+/* Fallback escalation (quantize.py:823-829): G64 = fp64 copy of G, then
+ * diag(G64) += extra * mean(diag(G64)). */
+int exl3b_convert_f32_f64(const float* dA, double* dB, size_t n, void* stream);
+int exl3b_damp_hessian_f64(double* dG, int k, double extra, void* stream);
+
+/* quantize() harness transposes (quantize.py:933-942, 961-965):
+ *   inverse = 0: Y[k][n] = X[n][k] / (row_mag[n] * col_mag[k])
+ *   inverse = 1: Y[n][k] = (X[k][n] * (*d_scale)) * (row_mag[n] * col_mag[k])
+ * mags nullable (= 1); X is [rows_x][cols_x]; sumsq_parts as above
+ * ([ceil(rows_x/32) * ceil(cols_x/32)] fp64, nullable). */
+int exl3b_transpose_scale(int inverse, const float* dX, int rows_x, int cols_x,
+                          const float* d_row_mag, const float* d_col_mag,
+                          const float* d_scale, float* dY,
+                          double* d_sumsq_parts, void* stream);
+
+/* *d_scale = fl32(sqrt(fl32(sum(parts) / count))) / lut_rms
+ * (quantize.py:803 / :941, fixed summation order). d_tmp: 1 fp64 scratch. */
+int exl3b_rms_scale(const double* d_parts, int nparts, double count,
+                    float lut_rms, double* d_tmp, float* d_scale, void* stream);
+
+/* y = x / *d_s elementwise (IEEE fp32 division), n a multiple of 4. */
+int exl3b_div_scalar(const float* dx, const float* d_s, float* dy, size_t n,
+                     void* stream);
+
+/* Block LDL (block_LDL, quantize.py:419-437): Cholesky of the SPD matrix A
+ * (fp32, or fp64 if f64; destroyed), 16x16 diagonal-block inverses,
+ * Lfac = L . blockdiag(DL^-1) with identity diagonal blocks, written as fp32
+ * [k][k] (the fp64 path's Lfac.float()).  dD (nullable) receives D blocks
+ * [k/16][16][16] in A's precision.  Synchronises `stream`; returns
+ * EXL3B_NOT_SPD if a pivot is not positive (quantize.py:815-835 fallback is
+ * the caller's). */
+size_t exl3b_block_ldl_workspace_bytes(int k, int f64);
+int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
+                    size_t ws_bytes, void* stream);
+
+/* quantize() U path (quantize.py:944-949): G = U^-1 U^-T in fp64 from an
+ * fp32 upper-triangular U [k][k]. */
+size_t exl3b_u_to_gram_workspace_bytes(int k);
+int exl3b_u_to_gram(const float* dU, int k, double* dG, void* ws,
+                    size_t ws_bytes, void* stream);
+
+/* BlockLDLQ sweep with fused tail-biting trellis encode (ldlq_viterbi,
+ * quantize.py:631-746, pack_states :360-378).
+ *   dWq   [k][n] fp32 unit-scaled inner weights
+ *   dLfac [k][k] fp32 block-LDL factor, or NULL (plain trellis encode)
+ *   segments: column tiles [seg_c0[s], seg_c0[s+1]) use K = seg_K[s] and write
+ *         trellis int16 [k/16][(seg_c0[s+1]-seg_c0[s])][16 K] at seg_trellis[s]
+ *         (seg_c0 has nseg+1 entries, seg_c0[0] = 0, seg_c0[nseg] = n/16;
+ *         up to 8 segments: one fused module with per-member K)
+ *   dHatW [k][n] fp32 decoded weights (output)
+ *   dStates [k/16][n/16][256] int32 (nullable), dXout [k/16][n/16][256]
+ *         fp32 encoder targets (nullable; for per-launch checks)
+ *   block_lo/block_hi: process k-blocks [block_lo, block_hi) (full sweep:
+ *         0, k/16); successive calls must walk downwards with the same ws
+ *   ws: exl3b_ldlq_workspace_bytes(k, n, min K, dLfac != NULL) bytes,
+ *         256-byte aligned; holds E = Wq - hatW, the feedback cache and the
+ *         encoder backpointers. */
+size_t exl3b_ldlq_workspace_bytes(int k, int n, int kmin, int use_ldlq);
+int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nseg,
+                     const int* seg_c0, const int* seg_K, int16_t* const* seg_trellis,
+                     int code, int pivot, int margin, int buf_cols, float* dHatW,
+                     int32_t* dStates, float* dXout, int block_lo, int block_hi,
+                     void* ws, size_t ws_bytes, void* stream);
+
+/* Bitstream (quantize.py:360-415): pack int32 states [ntiles][256] into
+ * int16 [ntiles][16K]; unpack back to full 16-bit states; decode a trellis
+ * [tk][tn][16K] to W_inner fp32 [16 tk][16 tn] through code `code`. */
+int exl3b_pack_states(const int32_t* dStates, int ntiles, int K, int16_t* dOut,
+                      void* stream);
+int exl3b_unpack_states(const int16_t* dTrellis, int ntiles, int K,
+                        int32_t* dStates, void* stream);
+int exl3b_decode_trellis(const int16_t* dTrellis, int tk, int tn, int K, int code,
+                         float* dW, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
