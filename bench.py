@@ -1,0 +1,379 @@
+#!/usr/bin/env python3
+"""bench.py -- EXL3 trellis quantizer throughput on B200.
+
+Metric: trellis-encoded weights/s (Viterbi + BlockLDLQ) at K=4.
+Workload (one "step"): quantize_linear of one configuration-2 projection --
+5120x5120 bf16 weight ~N(0, 0.02^2) with 0.1% outliers x10, Hessian from 4096
+synthetic heavy-tailed activation rows, random-sign Hadamard rotation, damped
+block-LDL, full BlockLDLQ sweep with the tail-biting trellis encode (K=4,
+mul1, quantize_linear defaults: pivot 128, margin 0), packing and W_hat.
+
+  value : weights/s with W and H resident in HBM (CUDA events around the
+          timed steps, max over ranks)
+  e2e   : same metric through the public API from pinned host buffers, the
+          host->device copy of W and H and the device->host copy of the
+          results inside every timed step
+  N > 1 : one process per GPU, each quantizing its own projection (seeded per
+          rank, no collective on the data path): weak scaling
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference algorithm's CPU implementation (the C/numpy
+restatement under oracle/; the reference itself is Python and does not travel)
+on the host cores: each step is one k-block launch of the same projection's
+LDLQ sweep (320 tiles), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "exl3xpu-mixedk_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "trellis-encoded weights/s (Viterbi+LDLQ) at K=4"
+UNIT = "weights/s"
+K_BITS = 4
+DIM = 5120
+OPS_PER_WEIGHT = 2 * 2 * 65536      # 2 passes x 2^16 ACS x 2 ops (margin 0)
+WORKLOAD = ("config 2: single dense projection 5120x5120 bf16 ~N(0,0.02^2) + 0.1% x10 "
+            "outliers; H = A^T A/4096, A Student-t(4) x lognormal(1) channel scales; "
+            "random-sign Hadamard, damped block-LDL, full BlockLDLQ + tail-biting "
+            "Viterbi K=4 mul1 (pivot 128, margin 0), pack, W_hat")
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def _measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def _profile_traffic():
+    """DRAM bytes per encoded weight of the tile kernel from the committed ncu
+    summary (line 'traffic_bytes_per_weight: N'), or None; scaled by the
+    weights one launch encodes."""
+    p = os.path.join(REPO, "profiles", "ldlq_tile_kernel_c2.md")
+    try:
+        txt = open(p).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_weight:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                idx = int(f[0])
+            except ValueError:
+                continue
+            if idx not in gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _cpu_sample(Wq, Lfac, lut, nblocks, warm=0, nthreads=None):
+    """Time `nblocks` k-blocks of the oracle sweep (after `warm` untimed ones);
+    returns (seconds per block list, threads)."""
+    from oracle import exl3_oracle as oracle
+    nth = nthreads or (os.cpu_count() or 1)
+    gen = oracle.ldlq_viterbi_steps(Wq, Lfac, lut, K_BITS, pivot=128, margin=0,
+                                    nthreads=nth)
+    times = []
+    for j in range(warm + nblocks):
+        t0 = time.perf_counter()
+        next(gen)
+        dt = time.perf_counter() - t0
+        if j >= warm:
+            times.append(dt)
+    return times, nth
+
+
+def _cpu_problem():
+    """Config-2 problem prepared by the oracle on the host (untimed)."""
+    import numpy as np
+    import torch
+    from exl3b import synth
+    from oracle import exl3_oracle as oracle
+    W, H = synth.config2(device="cuda")
+    W = W.float().cpu().numpy()
+    H = H.cpu().numpy()
+    lut = oracle.code_lut("exl3_mul1")
+    suh = oracle.sign_vec(DIM, 20261011).astype(np.float16)
+    svh = oracle.sign_vec(DIM, 20261012).astype(np.float16)
+    h = oracle.hadamard128()
+    Wi = oracle.to_inner(np.ascontiguousarray(W.T), suh, svh, h)
+    Wscale = np.float32(np.sqrt(np.float32(np.mean(Wi.astype(np.float64) ** 2)))) \
+        / oracle.lut_rms(lut)
+    Wq = (Wi / np.float32(Wscale)).astype(np.float32)
+    G = oracle.rotate_hessian(H, suh, h)
+    G[np.diag_indices_from(G)] += np.float32(0.01) * np.float32(np.mean(np.diagonal(G)))
+    Lfac, _ = oracle.block_LDL(G, 16)
+    del torch
+    return Wq, Lfac.astype(np.float32), lut
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    Wq, Lfac, lut = _cpu_problem()
+    times, nth = _cpu_sample(Wq, Lfac, lut, args.steps, warm=args.warmup)
+    per_block_w = (DIM // 16) * 256
+    t = sum(times) / len(times)
+    v = per_block_w / t
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "k": DIM, "n": DIM, "K": K_BITS,
+                   "step": "one k-block launch (320 tiles) of the sweep"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": nth, "kind": "port",
+                         "sample": f"{args.steps} consecutive k-blocks (320 tiles each, "
+                                   "right to left) of the config-2 LDLQ sweep after "
+                                   f"{args.warmup} warm-up blocks; one-off rotation and "
+                                   "LDL excluded (<1% of the CPU time)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--dim", type=int, default=DIM,
+                    help="projection size (default 5120 = config 2; smaller sizes are "
+                         "for profiler captures, not bench lines)")
+    args = ap.parse_args()
+    rank = _env_int("RANK", 0)
+    world = _env_int("WORLD_SIZE", 1)
+    local = _env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from exl3b import api, native, synth
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=dev)
+    L = native.lib()
+
+    if args.dim == DIM:
+        W, H = synth.config2(seed_w=1 + 100 * rank, seed_h=2 + 100 * rank, device=dev)
+    else:
+        W = synth.weight(args.dim, args.dim, 0.02, 1 + 100 * rank, dev)
+        H = synth.hessian(args.dim, 2 + 100 * rank, dev)
+    torch.cuda.synchronize()
+
+    def step():
+        return api.quantize_linear(W, H, K=K_BITS, device=dev, out_device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+    s = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n0 = L.exl3b_launch_count()
+    L.exl3b_profile_begin()
+    barrier()
+    e0.record(s)
+    for _ in range(args.steps):
+        r = step()
+    e1.record(s)
+    barrier()
+    import ctypes
+    ms_tile = ctypes.c_double(0.0)
+    n_tile = ctypes.c_longlong(0)
+    u_tile = ctypes.c_double(0.0)
+    native.check("exl3b_profile_end",
+                 L.exl3b_profile_end(0, ctypes.byref(ms_tile), ctypes.byref(n_tile),
+                                     ctypes.byref(u_tile)))
+    launches = (L.exl3b_launch_count() - n0) // args.steps
+    clocks = sampler.stop(set(range(max(world, 1)))) if sampler else None
+    ms = e0.elapsed_time(e1) / args.steps
+    t_max = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+    weights = args.dim * args.dim
+    value = world * weights / (ms / 1e3)
+
+    # ---- e2e: public API from pinned host buffers, copies inside the step
+    ms_e2e = float("nan")
+    h2d = d2h = 0
+    del r
+    if not args.no_e2e:
+        W_h = W.cpu().pin_memory()
+        H_h = H.cpu().pin_memory()
+        api.quantize_linear(W_h, H_h, K=K_BITS, device=dev, out_device="cpu")
+        barrier()
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record(s)
+        for _ in range(args.steps):
+            rr = api.quantize_linear(W_h, H_h, K=K_BITS, device=dev, out_device="cpu")
+        e3.record(s)
+        barrier()
+        ms_e2e = e2.elapsed_time(e3) / args.steps
+        h2d = W_h.numel() * W_h.element_size() + H_h.numel() * H_h.element_size()
+        d2h = sum(rr[k].numel() * rr[k].element_size()
+                  for k in ("W_hat", "trellis", "suh", "svh"))
+    t2 = torch.tensor([ms_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t2.item())
+
+    # ---- roofline of the dominant kernel (fused LDLQ tile kernel)
+    peaks = _measured_peaks()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    peak_ops = sms * 128 * mhz * 1e6 / 1e9           # Gop/s
+    tile_ms_avg = ms_tile.value / max(n_tile.value, 1)
+    w_per_launch = u_tile.value / max(n_tile.value, 1)
+    achieved = w_per_launch * OPS_PER_WEIGHT / (tile_ms_avg / 1e3) / 1e9
+    tpw = _profile_traffic()
+    roofline = {
+        "kernel": "ldlq_tile_kernel (fused feedback + tail-biting Viterbi + write-back)",
+        "bound": "alu", "achieved": achieved, "peak": peak_ops, "unit": "Gop/s",
+        "frac": achieved / peak_ops,
+        "peak_source": f"{sms} SMs x 128 lanes x {mhz:.0f} MHz (sm_max_mhz of "
+                       "MEASURED_PEAKS.json); 2 ops per add-compare-select",
+        "ops_per_weight": OPS_PER_WEIGHT,
+        "launches_per_step": n_tile.value / args.steps,
+        "avg_launch_ms": tile_ms_avg,
+        "share_of_step": ms_tile.value / args.steps / ms if ms else None,
+        "traffic": (tpw * w_per_launch) if tpw else None,
+        "traffic_unit": "bytes per launch",
+    }
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD if args.dim == DIM else f"{args.dim}x{args.dim} "
+                   "profiling case (not a bench line)", "k": args.dim, "n": args.dim,
+                   "K": K_BITS,
+                   "per_rank": "one projection per rank (seed 1+100r / 2+100r)",
+                   "l2": "inputs larger than L2 (W 52 MB bf16 + H 105 MB fp32 per step, "
+                         "plus ~1 GB of intermediates)",
+                   "parallelism": f"{world} independent ranks"},
+        "e2e": {"value": world * weights / (ms_e2e / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": ms_e2e},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "clocks": clocks,
+        "per_layer_s": ms / 1e3,
+    }
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.dim == DIM:
+        Wq, Lfac, lut = _cpu_problem()
+        times, nth = _cpu_sample(Wq, Lfac, lut, 2, warm=1)
+        t = sum(times) / len(times)
+        line["cpu_baseline"] = {
+            "value": (DIM // 16) * 256 / t, "unit": UNIT, "cores": nth, "kind": "port",
+            "sample": "2 k-blocks (320 tiles each) of the config-2 LDLQ sweep after 1 "
+                      "warm-up block, oracle C/numpy restatement, all host threads; "
+                      "one-off rotation and LDL excluded (<1% of CPU time)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -9,7 +9,9 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
+#include <vector>
 
 #include "exl3b_internal.h"
 #include "../../include/exl3b200.h"
@@ -31,6 +33,35 @@ int check_cuda(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return 0;
     set_error("%s: %s", what, cudaGetErrorString(e));
     return 1;
+}
+
+// ---------------------------------------------------------------- accounting
+static std::atomic<long long> g_launches{0};
+void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+struct ProfRec { cudaEvent_t a, b; int kind; double units; };
+static std::atomic<bool> g_prof{false};
+static std::mutex g_prof_mu;
+static std::vector<ProfRec> g_prof_recs;
+static ProfRec g_prof_open;
+
+bool prof_on() { return g_prof.load(std::memory_order_relaxed); }
+
+void prof_begin_launch(cudaStream_t s, int kind, double units) {
+    if (!prof_on()) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_open.kind = kind;
+    g_prof_open.units = units;
+    cudaEventCreate(&g_prof_open.a);
+    cudaEventCreate(&g_prof_open.b);
+    cudaEventRecord(g_prof_open.a, s);
+}
+
+void prof_end_launch(cudaStream_t s) {
+    if (!prof_on()) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    cudaEventRecord(g_prof_open.b, s);
+    g_prof_recs.push_back(g_prof_open);
 }
 
 // ---------------------------------------------------------------- codebooks
@@ -162,6 +193,35 @@ using namespace exl3b;
 extern "C" {
 
 const char* exl3b_last_error(void) { return g_err; }
+
+long long exl3b_launch_count(void) { return g_launches.load(); }
+
+void exl3b_profile_begin(void) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    for (auto& r : g_prof_recs) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
+    g_prof_recs.clear();
+    g_prof.store(true);
+}
+
+int exl3b_profile_end(int kind, double* ms_total, long long* launches, double* units) {
+    g_prof.store(false);
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    double ms = 0.0, u = 0.0;
+    long long n = 0;
+    for (auto& r : g_prof_recs) {
+        if (r.kind != kind) continue;
+        if (check_cuda(cudaEventSynchronize(r.b), "profile sync")) return RC_DEVICE_ERROR;
+        float e = 0.0f;
+        if (check_cuda(cudaEventElapsedTime(&e, r.a, r.b), "profile elapsed")) return RC_DEVICE_ERROR;
+        ms += e;
+        u += r.units;
+        ++n;
+    }
+    if (ms_total) *ms_total = ms;
+    if (launches) *launches = n;
+    if (units) *units = u;
+    return RC_OK;
+}
 
 int exl3b_abi_version(void) { return EXL3B_ABI_VERSION; }
 

@@ -26,6 +26,14 @@ struct DeviceState {
     size_t stage_seqs = 0;
 };
 
+// Kernel-launch accounting (exl3b_launch_count) and optional per-launch
+// CUDA-event timing of the dominant kernels (exl3b_profile_*).
+void note_launch(int n = 1);
+enum ProfKernel : int { PROF_TILE = 0, PROF_GEMM = 1, PROF_TAILBITE = 2, PROF_N = 3 };
+bool prof_on();
+void prof_begin_launch(cudaStream_t s, int kind, double units);
+void prof_end_launch(cudaStream_t s);
+
 // Current device's state, initialised on first use (rc != 0 on failure).
 int device_state(DeviceState** out);
 int device_sms();

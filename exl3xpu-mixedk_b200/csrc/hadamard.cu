@@ -180,6 +180,7 @@ int launch_had2(const HadParams& p, cudaStream_t stream) {
             set_error("input dtype id %d", p.in_dtype);
             return RC_BAD_REQUEST;
     }
+    note_launch();
     return check_cuda(cudaGetLastError(), "had2_kernel launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -210,6 +211,7 @@ int launch_row_rms(const void* X, int dtype, int rows, int cols, float* rms, cud
         case 2: row_rms_kernel<__half><<<grid, 256, 0, stream>>>((const __half*)X, rows, cols, rms); break;
         default: set_error("dtype %d", dtype); return RC_BAD_REQUEST;
     }
+    note_launch();
     return check_cuda(cudaGetLastError(), "row_rms launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -245,6 +247,7 @@ __global__ void chan_out_kernel(float* __restrict__ r_out, const float* __restri
 int launch_chan_out(float* r_out, const float* sv, int n, float* div_c, float* store_c,
                     cudaStream_t stream) {
     chan_out_kernel<<<1, 1024, 0, stream>>>(r_out, sv, n, div_c, store_c);
+    note_launch();
     return check_cuda(cudaGetLastError(), "chan_out launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -266,6 +269,7 @@ int launch_chan_in(const double* row_parts, int k, int nparts, const float* su, 
                    float* div_r, cudaStream_t stream) {
     chan_in_kernel<<<(k + 255) / 256, 256, 0, stream>>>(row_parts, k, nparts, nparts * 128,
                                                         su, r_in, div_r);
+    note_launch();
     return check_cuda(cudaGetLastError(), "chan_in launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -286,6 +290,7 @@ int launch_chan_store(const float* su, const float* r_in, const float* wscale,
     const int m = k > n ? k : n;
     chan_store_kernel<<<(m + 255) / 256, 256, 0, stream>>>(su, r_in, wscale, sv, store_c, k, n,
                                                            suh, svh);
+    note_launch();
     return check_cuda(cudaGetLastError(), "chan_store launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -348,6 +353,7 @@ int launch_transpose_scale(bool inv, const float* X, int rows_x, int cols_x,
     dim3 grid((cols_x + 31) / 32, (rows_x + 31) / 32);
     if (inv) transpose_scale_kernel<true><<<grid, 256, 0, stream>>>(X, rows_x, cols_x, rmag, cmag, s, Y, sumsq);
     else transpose_scale_kernel<false><<<grid, 256, 0, stream>>>(X, rows_x, cols_x, rmag, cmag, s, Y, sumsq);
+    note_launch();
     return check_cuda(cudaGetLastError(), "transpose_scale launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -391,6 +397,7 @@ int launch_rms_scale(const double* partials, int nparts, double count, float lut
                      double* tmp1, float* scale, cudaStream_t stream) {
     sum_f64_kernel<<<1, 1024, 0, stream>>>(partials, nparts, tmp1);
     rms_scale_kernel<<<1, 1, 0, stream>>>(tmp1, count, lut_rms, scale);
+    note_launch(2);
     return check_cuda(cudaGetLastError(), "rms_scale launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -401,6 +408,7 @@ int launch_div_scalar(const float* x, const float* s, float* y, size_t n, cudaSt
     if (grid > 148 * 16) grid = 148 * 16;
     div_scalar_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const float4*>(x), s,
                                                 reinterpret_cast<float4*>(y), n4);
+    note_launch();
     return check_cuda(cudaGetLastError(), "div_scalar launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -455,6 +463,7 @@ __global__ void damp_f64_kernel(double* __restrict__ G, int k, double extra) {
 
 int launch_damp_f64(double* G, int k, double extra, cudaStream_t stream) {
     damp_f64_kernel<<<1, 1024, 0, stream>>>(G, k, extra);
+    note_launch();
     return check_cuda(cudaGetLastError(), "damp_f64 launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -472,11 +481,13 @@ __global__ void count_nonfinite_kernel(const float* __restrict__ G, size_t n, in
 int launch_count_nonfinite(const float* G, size_t n, int* cnt, cudaStream_t stream) {
     cudaMemsetAsync(cnt, 0, sizeof(int), stream);
     count_nonfinite_kernel<<<148 * 4, 256, 0, stream>>>(G, n, cnt);
+    note_launch();
     return check_cuda(cudaGetLastError(), "count_nonfinite launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
 int launch_damp(float* G, int k, float percdamp, cudaStream_t stream) {
     damp_kernel<<<1, 1024, 0, stream>>>(G, k, percdamp, nullptr);
+    note_launch();
     return check_cuda(cudaGetLastError(), "damp launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 

@@ -210,17 +210,24 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
             for (int c0 = 0; c0 < tn; c0 += a.wave) {
                 const int nb = tn - c0 < a.wave ? tn - c0 : a.wave;
                 p.c_base = c0;
+                // profiling units: weights encoded by this launch
+                prof_begin_launch(stream, PROF_TILE, (double)nb * 256.0);
                 ldlq_tile_kernel<<<nb, kVT, smem, stream>>>(p);
+                prof_end_launch(stream);
+                note_launch();
                 if (check_cuda(cudaGetLastError(), "ldlq_tile_kernel launch"))
                     return RC_DEVICE_ERROR;
             }
         }
         if (a.Lfac && lo > 0 && lo >= a.block_lo) {
             // prod[0:16lo, :] += Lfac[16lo:16cur, 0:16lo]^T . E[16lo:16cur, :]
+            prof_begin_launch(stream, PROF_GEMM,
+                              (double)(16 * lo) * a.n * (16 * (cur - lo)) * 2.0);
             int rc = launch_gemm_tn_acc_f32(16 * lo, a.n, 16 * (cur - lo),
                                             a.Lfac + (size_t)16 * lo * a.k, a.k,
                                             a.E + (size_t)16 * lo * a.n, a.n,
                                             a.prod, a.n, stream);
+            prof_end_launch(stream);
             if (rc) return rc;
         }
     }
@@ -293,12 +300,14 @@ __global__ void decode_kernel(const int16_t* __restrict__ tr, int tk, int tn, in
 int launch_pack(const int32_t* st, int nt, int K, int16_t* out, cudaStream_t stream) {
     const size_t total = (size_t)nt * 8 * K;
     if (total) pack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(st, nt, K, out);
+    note_launch();
     return check_cuda(cudaGetLastError(), "pack launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
 int launch_unpack(const int16_t* tr, int nt, int K, int32_t* st, cudaStream_t stream) {
     const size_t total = (size_t)nt * 256;
     if (total) unpack_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(tr, nt, K, st);
+    note_launch();
     return check_cuda(cudaGetLastError(), "unpack launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -306,6 +315,7 @@ int launch_decode(const int16_t* tr, int tk, int tn, int K, const float* lut, fl
                   cudaStream_t stream) {
     const size_t total = (size_t)tk * tn * 256;
     if (total) decode_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(tr, tk, tn, K, lut, W);
+    note_launch();
     return check_cuda(cudaGetLastError(), "decode launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 

@@ -99,6 +99,7 @@ static int gemm_launch(int M, int N, int K, const T* A, int lda, const T* B, int
     gemm_kernel<T, A_KMAJ, B_KMAJ, LOWER, BM, BN, TM, TN>
         <<<grid, (BM / TM) * (BN / TN), 0, stream>>>(M, N, K, A, lda, B, ldb, C, ldc,
                                                     alpha, beta, status);
+    note_launch();
     return check_cuda(cudaGetLastError(), "gemm launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -215,9 +216,11 @@ int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream) {
                                                       T(-1), T(1), dstatus, stream);
             if (rc) return rc;
         }
+        note_launch(rest > 0 ? 2 : 1);
         if (check_cuda(cudaGetLastError(), "cholesky launch")) return RC_DEVICE_ERROR;
     }
     zero_upper_kernel<T><<<1024, 256, 0, stream>>>(A, n);
+    note_launch();
     return check_cuda(cudaGetLastError(), "zero_upper launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -299,6 +302,7 @@ int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream
     dl_inverse_kernel<T><<<n / 16, 256, 0, stream>>>(A, n, dDLi, dD);
     dim3 g((n + 255) / 256, n / 16);
     dl_apply_kernel<T><<<g, 256, 0, stream>>>(A, n, dDLi, Lout);
+    note_launch(2);
     return check_cuda(cudaGetLastError(), "block_ldl launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -334,11 +338,13 @@ int u_to_gram_f64(const float* U, int n, double* Ud, double* Ui, double* G, cuda
     int rc = gemm_launch<double, true, true, false>(n, n, n, Ui, n, Ui, n, G, n, 1.0, 0.0,
                                                     nullptr, stream);
     if (rc) return rc;
+    note_launch(2);
     return check_cuda(cudaGetLastError(), "u_to_gram launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
 int launch_f32_to_f64(const float* a, double* b, size_t n, cudaStream_t stream) {
     f32_to_f64_kernel<<<1024, 256, 0, stream>>>(a, b, n);
+    note_launch();
     return check_cuda(cudaGetLastError(), "f32_to_f64 launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 

@@ -41,6 +41,7 @@ int build_f2tab(int K, const __half* lut16, uint4* tab, cudaStream_t stream) {
         case 7: build_f2tab_kernel<7><<<1, kVT, 0, stream>>>(lut16, tab); break;
         default: set_error("K=%d outside 2..7", K); return RC_BAD_K;
     }
+    note_launch();
     return check_cuda(cudaGetLastError(), "build_f2tab launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
@@ -97,9 +98,12 @@ static int launch_k(const float* dX, int nseq, int pivot, int margin,
     }
     for (int s0 = 0; s0 < nseq; s0 += grid) {
         const int n = nseq - s0 < grid ? nseq - s0 : grid;
+        prof_begin_launch(stream, PROF_TAILBITE, (double)n * kSteps);
         tailbite_kernel<K><<<n, kVT, smem, stream>>>(
             dX + (size_t)s0 * kSteps, pivot, margin, dStates + (size_t)s0 * kSteps,
             ws, f2tab);
+        prof_end_launch(stream);
+        note_launch();
         if (check_cuda(cudaGetLastError(), "tailbite_kernel launch"))
             return RC_DEVICE_ERROR;
     }

@@ -182,7 +182,7 @@ def rotate_hessian(H_x: torch.Tensor, suh: torch.Tensor, h=None, device=None) ->
     dev = _cuda_device(device if device is not None else H_x.device)
     k = H_x.shape[0]
     _select(dev)
-    Hd = H_x.float().contiguous().to(dev)
+    Hd = H_x.float().contiguous().to(dev, non_blocking=True)
     su = suh.float().to(dev).contiguous()
     G = torch.empty(k, k, dtype=torch.float32, device=dev)
     call("exl3b_rotate_hessian", Hd.data_ptr(), k, su.data_ptr(), G.data_ptr(), _stream(dev))
@@ -455,7 +455,7 @@ def quantize_linear(W: torch.Tensor, H_x: torch.Tensor | None, code: str = "exl3
     lut_rms = _lut_rms(lut)
     suh = sign_vec(k_in, su_seed).half()
     svh = sign_vec(m_out, su_seed + 1).half()
-    W_dev = W.detach().to(dev)
+    W_dev = W.detach().to(dev, non_blocking=True)
     if W_dev.dtype not in DTYPE_IDS:
         W_dev = W_dev.float()
     W_dev = W_dev.contiguous()

@@ -34,6 +34,9 @@ SIGNATURES = {
     "exl3b_last_error": (ctypes.c_char_p, []),
     "exl3b_abi_version": (I, []),
     "exl3b_code_lut": (I, [I, P]),
+    "exl3b_launch_count": (ctypes.c_longlong, []),
+    "exl3b_profile_begin": (None, []),
+    "exl3b_profile_end": (I, [I, P, P, P]),
     "exl3b_device_init": (I, [I]),
     "exl3b_tailbite_workspace_bytes": (SZ, [I, I]),
     "exl3b_tailbite": (I, [P, I, I, I, I, I, P, P, SZ, P]),

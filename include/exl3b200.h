@@ -54,6 +54,19 @@ int exl3b_abi_version(void);
  * get_lut).  Needs no GPU. */
 int exl3b_code_lut(int code, float* out65536);
 
+/* Number of CUDA kernels this library has launched (all devices, all
+ * threads) since it was loaded. */
+long long exl3b_launch_count(void);
+
+/* Per-launch CUDA-event timing of the dominant kernels, on the stream each
+ * is launched on.  exl3b_profile_begin() starts recording; exl3b_profile_end
+ * stops, synchronises the recorded events and returns, for `kind`
+ * (0 = fused LDLQ tile kernel, 1 = feedback GEMM, 2 = standalone encoder),
+ * the summed duration, the launch count and the summed work units
+ * (0, 2: weights encoded; 1: FLOP). */
+void exl3b_profile_begin(void);
+int exl3b_profile_end(int kind, double* ms_total, long long* launches, double* units);
+
 /* Select `device` and build its decode tables (optional; first use of any
  * entry point initialises the current device). */
 int exl3b_device_init(int device);

@@ -280,14 +280,14 @@ def decode_trellis(trellis: np.ndarray, lut: np.ndarray, K: int, k: int,
 
 
 # ------------------------------------------------------------------ LDLQ sweep
-def ldlq_viterbi(Wq: np.ndarray, Lfac: np.ndarray | None, lut: np.ndarray,
-                 K: int, L: int = 16, buf_cols: int = 128,
-                 pivot: int | None = None, margin: int = 0,
-                 nthreads: int = 1, on_launch=None):
-    """quantize.py:631-746 BlockLDLQ sweep (right to left over 16-row k-blocks,
-    128-row buffers).  Wq [k, n] fp32 -> (hatW [k, n] fp32,
-    states int64 [k/16, n/16, 256]).  on_launch(i, X[tn, 256], states) is
-    called per k-block (the per-launch hook of quantize.py:687-717)."""
+def ldlq_viterbi_steps(Wq: np.ndarray, Lfac: np.ndarray | None, lut: np.ndarray,
+                       K: int, L: int = 16, buf_cols: int = 128,
+                       pivot: int | None = None, margin: int = 0,
+                       nthreads: int = 1, on_launch=None):
+    """Generator form of quantize.py:631-746: yields the k-block index after
+    each block (right to left), finally returns (hatW [k, n] fp32,
+    states int64 [k/16, n/16, 256]) as the StopIteration value.  Each block
+    is one launch of the reference's sweep (tn tiles)."""
     k, n = Wq.shape
     perm = tensor_core_perm()
     kp, np_ = perm // 16, perm % 16
@@ -321,11 +321,29 @@ def ldlq_viterbi(Wq: np.ndarray, Lfac: np.ndarray | None, lut: np.ndarray,
             tiles[:, perm] = vals
             hatW_t[:, c0:c1] = tiles.reshape(tn, 16, 16).transpose(1, 0, 2) \
                 .reshape(16, n).T
+            yield i
         if not no_ldlq and lo > 0:
             prod += Lfac[16 * lo:16 * cur, :].T @ \
                 (W_t[:, 16 * lo:16 * cur] - hatW_t[:, 16 * lo:16 * cur]).T
     return np.ascontiguousarray(hatW_t.T), np.ascontiguousarray(
         states.transpose(1, 0, 2))
+
+
+def ldlq_viterbi(Wq: np.ndarray, Lfac: np.ndarray | None, lut: np.ndarray,
+                 K: int, L: int = 16, buf_cols: int = 128,
+                 pivot: int | None = None, margin: int = 0,
+                 nthreads: int = 1, on_launch=None):
+    """quantize.py:631-746 BlockLDLQ sweep (right to left over 16-row k-blocks,
+    128-row buffers).  Wq [k, n] fp32 -> (hatW [k, n] fp32,
+    states int64 [k/16, n/16, 256]).  on_launch(i, X[tn, 256], states) is
+    called per k-block (the per-launch hook of quantize.py:687-717)."""
+    gen = ldlq_viterbi_steps(Wq, Lfac, lut, K, L, buf_cols, pivot, margin,
+                             nthreads, on_launch)
+    while True:
+        try:
+            next(gen)
+        except StopIteration as e:
+            return e.value
 
 
 # ------------------------------------------------------------------ top level
