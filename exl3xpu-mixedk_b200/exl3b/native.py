@@ -40,6 +40,7 @@ SIGNATURES = {
     "exl3b_device_init": (I, [I]),
     "exl3b_tailbite_workspace_bytes": (SZ, [I, I]),
     "exl3b_tailbite": (I, [P, I, I, I, I, I, P, P, SZ, P]),
+    "exl3b_tailbite_noalloc": (I, [P, I, I, I, I, I, P, P]),
     "xtq_vit_init": (I, []),
     "xtq_vit_run": (I, [P, I, ctypes.c_char_p, I, I, P]),
     "exl3b_incoherence_fwd": (I, [P, I, I, I, P, P, P, P, P]),

@@ -88,6 +88,24 @@ int exl3b_tailbite(const float* dX, int nseq, int K, int code, int pivot,
                    int margin, int32_t* dStates, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/* Tail-biting encode that allocates no device memory.  No counterpart in the
+ * reference: it is for callers that must not allocate device memory while
+ * they run -- a process whose GPU memory belongs to another allocator (for
+ * example an inference server that reserves the device's memory at start-up
+ * and treats later cudaMalloc calls as failures), or a loop that cannot take
+ * the device-wide synchronisation cudaMalloc / cudaFree can cause.  Same
+ * arguments and results as exl3b_tailbite, minus the workspace: the
+ * backpointer scratch is a fixed 64 MiB device array inside the library
+ * (held by every GPU that loads it until exit) and the decode values are
+ * computed from the code formulas.  At most 64 (K = 2, 3), 128 (K = 4, 5),
+ * 256 (K = 6) or 512 (K = 7) sequences per call; more returns
+ * EXL3B_BAD_NSEQ.  All calls on a device share the scratch: calls that
+ * overlap on the GPU race, so issue them in order on one stream.  The first
+ * call on a device looks up the scratch address and sets kernel attributes
+ * (no allocation); make it before any stream capture. */
+int exl3b_tailbite_noalloc(const float* dX, int nseq, int K, int code, int pivot,
+                           int margin, int32_t* dStates, void* stream);
+
 /* Drop-in for the reference's native Viterbi (viterbi_esimd.cpp:935-1005):
  * same signatures, argument meaning and return codes.  Host X [nseq][256]
  * fp32 in, host int32 states [nseq][256] out, synchronous, mul1 code at
