@@ -243,10 +243,9 @@ int exl3b_u_to_gram(const float* dU, int k, double* dG, void* ws, size_t ws_byte
 
 
 // ------------------------------------------------------------------ LDLQ
-static int sweep_wave(int tn) {
-    const int sms = device_sms();
-    return tn < sms ? tn : sms;
-}
+// Workspace: E [k][n] | prod [k][n] (LDLQ only) | backpointer slots |
+// control words (slot flags, per-column progress, ticket, error word).
+static int sweep_slots() { return device_sms() * ldlq_tile_max_resident_per_sm() + 16; }
 
 static size_t sweep_slot(const int* seg_K, int nseg) {
     size_t m = 0;
@@ -257,11 +256,16 @@ static size_t sweep_slot(const int* seg_K, int nseg) {
     return m;
 }
 
+static size_t sweep_ctrl_bytes(int tn) {
+    return align256(((size_t)sweep_slots() + (size_t)tn + 24) * sizeof(int));
+}
+
 size_t exl3b_ldlq_workspace_bytes(int k, int n, int kmin, int use_ldlq) {
     if (k <= 0 || n <= 0 || k % 16 || n % 16 || kmin < 2 || kmin > 7) return 0;
     const size_t kn = (size_t)k * n * 4;
-    const size_t bp = (size_t)sweep_wave(n / 16) * bp_slot_bytes(kmin);
-    return align256(kn) + (use_ldlq ? align256(kn) : 0) + align256(bp);
+    const size_t bp = (size_t)sweep_slots() * bp_slot_bytes(kmin);
+    return align256(kn) + (use_ldlq ? align256(kn) : 0) + align256(bp) +
+           sweep_ctrl_bytes(n / 16);
 }
 
 int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nseg,
@@ -315,10 +319,18 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     uint8_t* w = static_cast<uint8_t*>(ws);
     const size_t kn = align256((size_t)k * n * 4);
     a.E = reinterpret_cast<float*>(w);
-    a.prod = dLfac ? reinterpret_cast<float*>(w + kn) : nullptr;
-    a.bp_ws = w + kn + (dLfac ? kn : 0);
+    w += kn;
+    a.prod = dLfac ? reinterpret_cast<float*>(w) : nullptr;
+    if (dLfac) w += kn;
+    a.nslots = sweep_slots();
     a.bp_slot = sweep_slot(seg_K, nseg);
-    a.wave = sweep_wave(tn);
+    a.bp_ws = w;
+    w += align256((size_t)a.nslots * bp_slot_bytes(kmin));
+    int* ctrl = reinterpret_cast<int*>(w);
+    a.slots = ctrl;
+    a.colprog = ctrl + a.nslots;
+    a.tickets = a.colprog + tn;
+    a.err = a.tickets + 1;
     a.Wq = dWq; a.Lfac = dLfac; a.k = k; a.n = n;
     a.nseg = nseg; a.seg_c0 = seg_c0; a.seg_K = seg_K; a.seg_trellis = seg_trellis;
     a.pivot = pivot; a.margin = margin; a.buf_cols = buf_cols;
@@ -326,10 +338,30 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     a.f2tab = tabs; a.lut32 = st->lut32[code];
     a.block_lo = block_lo; a.block_hi = block_hi;
     cudaStream_t s = S(stream);
-    if (dLfac && block_hi == tk &&
-        check_cuda(cudaMemsetAsync(a.prod, 0, (size_t)k * n * 4, s), "memset prod"))
+    if (block_hi == tk) {   // start of a sweep: feedback cache and control words
+        if ((dLfac && check_cuda(cudaMemsetAsync(a.prod, 0, (size_t)k * n * 4, s), "memset prod")) ||
+            check_cuda(cudaMemsetAsync(ctrl, 0, sweep_ctrl_bytes(tn), s), "memset control"))
+            return RC_DEVICE_ERROR;
+    }
+    int rc = ldlq_sweep(a, s);
+    if (rc) return rc;
+    // the tile kernels bound every dependency wait; report a time-out
+    int err[14] = {};
+    if (check_cuda(cudaMemcpyAsync(err, a.err, sizeof(err), cudaMemcpyDeviceToHost, s),
+                   "read sweep status") ||
+        check_cuda(cudaStreamSynchronize(s), "sweep sync"))
         return RC_DEVICE_ERROR;
-    return ldlq_sweep(a, s);
+    if (err[0]) {
+        set_error("LDLQ sweep: tile scheduling failed (%s) at ticket %d, k-block %d, "
+                  "column %d, column progress %d; slots held %d of %d, first holders "
+                  "%d %d %d %d %d %d %d %d",
+                  err[0] == 1 ? "no free backpointer slot" :
+                  err[0] == 2 ? "dependency wait timed out" : "aborted", err[1], err[2],
+                  err[3], err[4], err[13], a.nslots, err[5], err[6], err[7], err[8], err[9],
+                  err[10], err[11], err[12]);
+        return RC_DEVICE_ERROR;
+    }
+    return RC_OK;
 }
 
 int exl3b_pack_states(const int32_t* dStates, int ntiles, int K, int16_t* dOut, void* stream) {

@@ -122,12 +122,17 @@ struct SweepArgs {
     float* xout;
     uint8_t* bp_ws;
     size_t bp_slot;
-    int wave;                // CTAs per wave (= bp slots)
+    int nslots;              // backpointer slots (> SM count)
+    int* slots;              // [nslots] ownership flags (zero at sweep start)
+    int* colprog;            // [tn] finished k-blocks per column (zero at start)
+    int* tickets;            // launch ticket counter (zeroed before each launch)
+    int* err;                // error word (zero at sweep start)
     const uint4* const* f2tab;  // [8] per K
     const float* lut32;
     int block_hi, block_lo;  // sweep blocks [block_lo, block_hi)
 };
 int ldlq_sweep(const SweepArgs& a, cudaStream_t stream);
+int ldlq_tile_max_resident_per_sm();
 int launch_pack(const int32_t* st, int nt, int K, int16_t* out, cudaStream_t stream);
 int launch_unpack(const int16_t* tr, int nt, int K, int32_t* st, cudaStream_t stream);
 int launch_decode(const int16_t* tr, int tk, int tn, int K, const float* lut, float* W,

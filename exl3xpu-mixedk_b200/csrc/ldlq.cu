@@ -10,10 +10,16 @@
 //   trellis int16 [k/16][n_seg/16][16K] per column segment (output)
 //
 // Sweep (host loop, all launches on one stream): k-blocks right to left in
-// 128-row buffers; per k-block one tile kernel over its column tiles (waves
-// of at most one CTA per SM); after a buffer, prod[:16lo] += Lfac[buf, :16lo]^T
-// E[buf].  Columns never interact (Lfac couples rows only), so each CTA owns
-// one column tile of the current k-block:
+// 128-row buffers.  One tile-kernel launch per buffer covers all its k-blocks x
+// column tiles: each CTA takes a ticket in dependency order (k-block
+// descending, column ascending) and, when it needs the block below it in the
+// same column (intra-buffer feedback), waits on that column's progress
+// counter.  The producer of that block took an earlier ticket, so it is
+// resident and finishes: no deadlock, and no wave quantisation (320 column
+// tiles on 148 SMs would otherwise leave the third wave 84% idle).  The wait is
+// bounded; on time-out the CTA sets an error word and returns.  After a
+// buffer, prod[:16lo] += Lfac[buf, :16lo]^T E[buf].  Columns never interact
+// (Lfac couples rows only), so each CTA owns one column tile of one k-block:
 //   WXWX = (Wq + Lfac[later, blk]^T . E[later]) + prod     (quantize.py:676-682)
 //   x[t] = WXWX[perm[t]]                                   (:684-686)
 //   states = tail-biting encode(x)                         (:687-731)
@@ -35,14 +41,23 @@ struct LdlqTileParams {
     const float* Lfac;      // null: no feedback
     const float* prod;      // null: no feedback
     int k, n;
-    int i;                  // k-block
     int cur;                // buffer end block (exclusive)
-    int c_base;             // first column tile of this wave
+    int top;                // first (highest) k-block of this launch
+    int tk;                 // k-blocks of the whole matrix
     int pivot, margin;
+    int* tickets;           // launch ticket counter (zeroed before launch)
+    int* colprog;           // [tn] k-blocks finished per column (sweep-wide)
+    int* slots;             // [nslots] backpointer-slot ownership flags
+    int nslots;
+    int* err;               // error word (set on a wait time-out)
     int nseg;
     int seg_c0[kMaxSeg + 1];     // segment column-tile starts, seg_c0[nseg] = tn
     int seg_K[kMaxSeg];
     int16_t* seg_trellis[kMaxSeg];
+    // segments encoded by this launch (all of one K): ids and column prefix
+    int nls;
+    int ls_seg[kMaxSeg];
+    int ls_pre[kMaxSeg + 1];     // ls_pre[m] = columns of segments ls_seg[0..m)
     int32_t* states;        // [tk][tn][256] or null
     float* xout;            // [tk][tn][256] or null (encoder targets, for checks)
     uint8_t* bp_ws;         // wave slots
@@ -60,9 +75,13 @@ __device__ __forceinline__ int tc_perm(int t) {
     return row * 16 + col;
 }
 
+// sched (shared): [0] k-block i, [1] column tile c, [2] backpointer slot,
+// [3] ok, [4] column segment.  Re-read where needed instead of being kept
+// live in registers across the encode.
 template <int K>
 __device__ __forceinline__ void ldlq_tile_body(const LdlqTileParams& p, char* smem,
-                                               int c, int seg) {
+                                               const volatile int* sched) {
+    int i = sched[0], c = sched[1], seg;
     using SM = VitSmem<K>;
     const int t = threadIdx.x;
     float* xs = reinterpret_cast<float*>(smem + SM::OFF_X);
@@ -73,15 +92,19 @@ __device__ __forceinline__ void ldlq_tile_body(const LdlqTileParams& p, char* sm
     // ---- feedback: WXWX tile
     if (t < 256) {
         const int a = t >> 4, col = t & 15;
-        const size_t row = (size_t)(16 * p.i + a);
+        const size_t row = (size_t)(16 * i + a);
         const size_t gc = (size_t)(16 * c + col);
         float w = p.Wq[row * n + gc];
         if (p.Lfac) {
-            const int r_lo = 16 * (p.i + 1), r_hi = 16 * p.cur;
+            const int r_lo = 16 * (i + 1), r_hi = 16 * p.cur;
             if (r_lo < r_hi) {
+                // E rows of this buffer were written by other CTAs of this
+                // launch: read them at L2 (ld.global.cg), never from a
+                // possibly stale L1 line shared with a neighbouring column
                 float acc = 0.0f;
                 for (int r = r_lo; r < r_hi; ++r)
-                    acc = fmaf(p.Lfac[(size_t)r * p.k + 16 * p.i + a], p.E[(size_t)r * n + gc], acc);
+                    acc = fmaf(p.Lfac[(size_t)r * p.k + 16 * i + a],
+                               __ldcg(&p.E[(size_t)r * n + gc]), acc);
                 w = w + acc;
             }
             w = w + p.prod[row * n + gc];
@@ -92,7 +115,7 @@ __device__ __forceinline__ void ldlq_tile_body(const LdlqTileParams& p, char* sm
     if (t < 256) {
         const float x = wx[tc_perm(t)];
         xs[t] = x;
-        if (p.xout) p.xout[((size_t)p.i * tn + c) * 256 + t] = x;
+        if (p.xout) p.xout[((size_t)i * tn + c) * 256 + t] = x;
     }
     __syncthreads();
 
@@ -100,20 +123,25 @@ __device__ __forceinline__ void ldlq_tile_body(const LdlqTileParams& p, char* sm
     {
         __half2 f2[64];
         vit_load_f2tab(f2, p.f2tab[K], t);
-        uint8_t* bp = p.bp_ws + (size_t)blockIdx.x * p.bp_slot;
+        uint8_t* bp = p.bp_ws + (size_t)sched[2] * p.bp_slot;
         vit_tailbite<K>(f2, smem, p.pivot, p.margin, bp, t);
     }
 
-    // ---- write-back: decoded tile, error, states
+    // ---- write-back: decoded tile, error, states.  The column tile and its
+    // segment are recomputed from the launch parameters here rather than kept
+    // live in registers across the encode.
+    i = sched[0];
+    c = sched[1];
+    seg = sched[4];
     const int32_t* st = reinterpret_cast<const int32_t*>(smem + SM::OFF_ST);
     if (t < 256) {
         const int s = st[t];
         const int pos = tc_perm(t);
-        const size_t idx = (size_t)(16 * p.i + (pos >> 4)) * n + (size_t)(16 * c + (pos & 15));
+        const size_t idx = (size_t)(16 * i + (pos >> 4)) * n + (size_t)(16 * c + (pos & 15));
         const float v = p.lut32[s];
         p.hatW[idx] = v;
         p.E[idx] = p.Wq[idx] - v;
-        if (p.states) p.states[((size_t)p.i * tn + c) * 256 + t] = s;
+        if (p.states) p.states[((size_t)i * tn + c) * 256 + t] = s;
     }
     // ---- pack: stream bit q = t*K + b (MSB first within a symbol); u32 word
     // w holds stream bits [32w, 32w+32) MSB first; stored as int16 low half
@@ -130,44 +158,164 @@ __device__ __forceinline__ void ldlq_tile_body(const LdlqTileParams& p, char* sm
         }
         const int seg_tn = p.seg_c0[seg + 1] - p.seg_c0[seg];
         int16_t* out = p.seg_trellis[seg] +
-                       ((size_t)p.i * seg_tn + (c - p.seg_c0[seg])) * (16 * K);
+                       ((size_t)i * seg_tn + (c - p.seg_c0[seg])) * (16 * K);
         out[2 * t] = (int16_t)(word & 0xFFFFu);
         out[2 * t + 1] = (int16_t)(word >> 16);
     }
 }
 
+__device__ __forceinline__ int ld_acquire(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+constexpr long long kWaitNs = 4000000000LL;   // 4 s bound on any dependency wait
+
+// slot-holder tag: (SM id << 20) | (ticket + 1), nonzero
+__device__ __forceinline__ int holder_tag(int ticket) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    return (int)((smid << 20) | (unsigned)((ticket + 1) & 0xFFFFF));
+}
+
+template <int K>
 __global__ void __launch_bounds__(kVT, 1)
 ldlq_tile_kernel(const __grid_constant__ LdlqTileParams p) {
     extern __shared__ __align__(16) char smem[];
-    const int c = p.c_base + blockIdx.x;
-    int seg = 0;
-    while (seg + 1 < p.nseg && c >= p.seg_c0[seg + 1]) ++seg;
-    switch (p.seg_K[seg]) {
-        case 2: ldlq_tile_body<2>(p, smem, c, seg); break;
-        case 3: ldlq_tile_body<3>(p, smem, c, seg); break;
-        case 4: ldlq_tile_body<4>(p, smem, c, seg); break;
-        case 5: ldlq_tile_body<5>(p, smem, c, seg); break;
-        case 6: ldlq_tile_body<6>(p, smem, c, seg); break;
-        case 7: ldlq_tile_body<7>(p, smem, c, seg); break;
-        default: break;
+    __shared__ int sched[5];            // i, c, slot, ok, segment
+    const int t = threadIdx.x;
+    if (t == 0) {
+        const int ncols = p.ls_pre[p.nls];
+        const int ticket = atomicAdd(p.tickets, 1);
+        const int i = p.top - ticket / ncols;
+        const int lc = ticket % ncols;
+        int m = 0;
+        while (m + 1 < p.nls && lc >= p.ls_pre[m + 1]) ++m;
+        const int seg = p.ls_seg[m];
+        const int c = p.seg_c0[seg] + (lc - p.ls_pre[m]);
+        int ok = 1;
+        // backpointer slot: nslots exceeds the CTAs the device can hold
+        // resident at once (SMs x occupancy), so at every instant a slot is
+        // free.  CTAs of a wave start together and race for the slots their
+        // predecessors just released, so a single pass can lose every race:
+        // keep scanning (hashed start, read before CAS) until one is won,
+        // within the same time bound as the dependency wait.
+        int slot = -1;
+        int cause = 0, seen = -1;
+        {
+            const unsigned h = (unsigned)ticket * 2654435761u;
+            const int start = (int)(h % (unsigned)p.nslots);
+            const long long t0 = clock64();
+            const long long limit = (long long)(kWaitNs * 2.0);
+            while (slot < 0) {
+                for (int k = 0; k < p.nslots && slot < 0; ++k) {
+                    int cand = start + k;
+                    if (cand >= p.nslots) cand -= p.nslots;
+                    if (ld_acquire(&p.slots[cand]) == 0 &&
+                        atomicCAS(&p.slots[cand], 0, holder_tag(ticket)) == 0)
+                        slot = cand;
+                }
+                if (slot >= 0) break;
+                if (clock64() - t0 > limit) break;
+                __nanosleep(128);
+            }
+        }
+        if (slot < 0) { ok = 0; cause = 1; }
+        // intra-buffer feedback needs blocks i+1 .. cur-1 of this column
+        if (ok && p.Lfac && i + 1 < p.cur) {
+            const int need = p.tk - 1 - i;
+            const long long t0 = clock64();
+            const long long limit = (long long)(kWaitNs * 2.0);   // cycles at <= 2 GHz
+            while ((seen = ld_acquire(&p.colprog[c])) < need) {
+                if (ld_acquire(p.err)) { ok = 0; break; }
+                if (clock64() - t0 > limit) { ok = 0; cause = 2; break; }
+                __nanosleep(256);
+            }
+        }
+        if (!ok && cause) {
+            // first failure records what it was: cause (1 slot, 2 wait),
+            // ticket, k-block, column, progress seen
+            if (atomicCAS(p.err, 0, cause) == 0) {
+                p.err[1] = ticket; p.err[2] = i; p.err[3] = c; p.err[4] = seen;
+                // holders (ticket + 1) of the first slots, for diagnosis
+                for (int q = 0; q < 8; ++q) p.err[5 + q] = p.slots[q];
+                int held = 0;
+                for (int q = 0; q < p.nslots; ++q) held += p.slots[q] != 0;
+                p.err[13] = held;
+            }
+        } else if (!ok) {
+            atomicCAS(p.err, 0, 3);
+        }
+        sched[0] = i;
+        sched[1] = c;
+        sched[2] = slot;
+        sched[3] = ok;
+        sched[4] = seg;
+    }
+    __syncthreads();
+    if (!sched[3]) {
+        if (t == 0 && sched[2] >= 0) atomicExch(&p.slots[sched[2]], 0);
+        return;
+    }
+    ldlq_tile_body<K>(p, smem, sched);
+    __syncthreads();    // every thread's writes of this tile precede the release
+    if (t == 0) {
+        __threadfence();
+        atomicExch(&p.slots[sched[2]], 0);
+        atomicAdd(&p.colprog[sched[1]], 1);
     }
 }
 
-static int max_smem_for(const int* Ks, int nseg) {
-    int m = 0;
-    for (int s = 0; s < nseg; ++s) {
-        int b = 0;
-        switch (Ks[s]) {
-            case 2: b = VitSmem<2>::BYTES; break;
-            case 3: b = VitSmem<3>::BYTES; break;
-            case 4: b = VitSmem<4>::BYTES; break;
-            case 5: b = VitSmem<5>::BYTES; break;
-            case 6: b = VitSmem<6>::BYTES; break;
-            case 7: b = VitSmem<7>::BYTES; break;
-        }
-        m = b > m ? b : m;
+template <int K>
+static int launch_tile_k(const LdlqTileParams& p, unsigned grid, cudaStream_t stream) {
+    static bool attr[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev]) {
+        if (check_cuda(cudaFuncSetAttribute(ldlq_tile_kernel<K>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            VitSmem<K>::BYTES),
+                       "cudaFuncSetAttribute(ldlq_tile)"))
+            return RC_DEVICE_ERROR;
+        attr[dev] = true;
     }
+    ldlq_tile_kernel<K><<<grid, kVT, VitSmem<K>::BYTES, stream>>>(p);
+    note_launch();
+    return check_cuda(cudaGetLastError(), "ldlq_tile_kernel launch") ? RC_DEVICE_ERROR : RC_OK;
+}
+
+// Most CTAs of the K=2..7 tile kernels one SM can hold at once (driver
+// occupancy calculation), cached per device.  Sizes the backpointer-slot pool.
+int ldlq_tile_max_resident_per_sm() {
+    static int cache[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cache[dev]) return cache[dev];
+    int m = 1, nb = 0;
+#define EXL3B_OCC(K)                                                                   \
+    cudaFuncSetAttribute(ldlq_tile_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                         VitSmem<K>::BYTES);                                           \
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, ldlq_tile_kernel<K>, kVT,    \
+                                                      VitSmem<K>::BYTES) == cudaSuccess \
+        && nb > m) m = nb;
+    EXL3B_OCC(2) EXL3B_OCC(3) EXL3B_OCC(4) EXL3B_OCC(5) EXL3B_OCC(6) EXL3B_OCC(7)
+#undef EXL3B_OCC
+    cache[dev] = m;
     return m;
+}
+
+static int launch_tile(int K, const LdlqTileParams& p, unsigned grid, cudaStream_t stream) {
+    switch (K) {
+        case 2: return launch_tile_k<2>(p, grid, stream);
+        case 3: return launch_tile_k<3>(p, grid, stream);
+        case 4: return launch_tile_k<4>(p, grid, stream);
+        case 5: return launch_tile_k<5>(p, grid, stream);
+        case 6: return launch_tile_k<6>(p, grid, stream);
+        case 7: return launch_tile_k<7>(p, grid, stream);
+    }
+    set_error("K=%d outside 2..7", K);
+    return RC_BAD_K;
 }
 
 int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
@@ -176,57 +324,65 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
     memset(&p, 0, sizeof(p));
     p.Wq = a.Wq; p.E = a.E; p.hatW = a.hatW; p.Lfac = a.Lfac;
     p.prod = a.Lfac ? a.prod : nullptr;
-    p.k = a.k; p.n = a.n; p.pivot = a.pivot; p.margin = a.margin;
+    p.k = a.k; p.n = a.n; p.pivot = a.pivot; p.margin = a.margin; p.tk = tk;
     p.nseg = a.nseg;
     for (int s = 0; s <= a.nseg; ++s) p.seg_c0[s] = a.seg_c0[s];
     for (int s = 0; s < a.nseg; ++s) { p.seg_K[s] = a.seg_K[s]; p.seg_trellis[s] = a.seg_trellis[s]; }
     p.states = a.states; p.xout = a.xout; p.bp_ws = a.bp_ws; p.bp_slot = a.bp_slot;
+    p.slots = a.slots; p.nslots = a.nslots; p.colprog = a.colprog; p.err = a.err;
     for (int K = 0; K < 8; ++K) p.f2tab[K] = a.f2tab[K];
     p.lut32 = a.lut32;
 
-    const int smem = max_smem_for(a.seg_K, a.nseg);
-    static bool attr[kMaxDevices] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr[dev]) {
-        if (check_cuda(cudaFuncSetAttribute(ldlq_tile_kernel,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            VitSmem<2>::BYTES),
-                       "cudaFuncSetAttribute(ldlq_tile)"))
-            return RC_DEVICE_ERROR;
-        attr[dev] = true;
+    // k-blocks [lo, hi) of buffer end `cur`: one launch per distinct K over the
+    // column segments of that K
+    auto launch = [&](int cur, int lo, int hi) -> int {
+        p.cur = cur;
+        p.top = hi - 1;
+        p.tickets = a.tickets;
+        bool done[kMaxSeg] = {};
+        for (int s0 = 0; s0 < a.nseg; ++s0) {
+            if (done[s0]) continue;
+            const int K = a.seg_K[s0];
+            p.nls = 0;
+            p.ls_pre[0] = 0;
+            for (int s1 = s0; s1 < a.nseg; ++s1) {
+                if (a.seg_K[s1] != K) continue;
+                done[s1] = true;
+                p.ls_seg[p.nls] = s1;
+                p.ls_pre[p.nls + 1] = p.ls_pre[p.nls] + (a.seg_c0[s1 + 1] - a.seg_c0[s1]);
+                ++p.nls;
+            }
+            if (check_cuda(cudaMemsetAsync(a.tickets, 0, sizeof(int), stream), "memset tickets"))
+                return RC_DEVICE_ERROR;
+            const long long nb = (long long)(hi - lo) * p.ls_pre[p.nls];
+            prof_begin_launch(stream, PROF_TILE, (double)nb * 256.0);
+            const int rc = launch_tile(K, p, (unsigned)nb, stream);
+            prof_end_launch(stream);
+            if (rc) return rc;
+        }
+        return RC_OK;
+    };
+    if (!a.Lfac) {
+        // no feedback: every tile is independent, one launch
+        return launch(a.block_hi, a.block_lo, a.block_hi);
     }
     const int buf_tiles = a.buf_cols / 16 > 0 ? a.buf_cols / 16 : 1;
     // buffers are anchored at tk like the reference: [tk - 8m - 8, tk - 8m)
     for (int cur = tk; cur > 0; cur -= buf_tiles) {
         const int lo = cur - buf_tiles > 0 ? cur - buf_tiles : 0;
-        if (lo >= a.block_hi || cur <= a.block_lo) {
-            continue;
-        }
-        p.cur = cur;
-        for (int i = cur - 1; i >= lo; --i) {
-            if (i >= a.block_hi || i < a.block_lo) continue;
-            p.i = i;
-            for (int c0 = 0; c0 < tn; c0 += a.wave) {
-                const int nb = tn - c0 < a.wave ? tn - c0 : a.wave;
-                p.c_base = c0;
-                // profiling units: weights encoded by this launch
-                prof_begin_launch(stream, PROF_TILE, (double)nb * 256.0);
-                ldlq_tile_kernel<<<nb, kVT, smem, stream>>>(p);
-                prof_end_launch(stream);
-                note_launch();
-                if (check_cuda(cudaGetLastError(), "ldlq_tile_kernel launch"))
-                    return RC_DEVICE_ERROR;
-            }
-        }
-        if (a.Lfac && lo > 0 && lo >= a.block_lo) {
+        const int hi_l = cur < a.block_hi ? cur : a.block_hi;
+        const int lo_l = lo > a.block_lo ? lo : a.block_lo;
+        if (lo_l >= hi_l) continue;
+        int rc = launch(cur, lo_l, hi_l);
+        if (rc) return rc;
+        if (lo > 0 && lo >= a.block_lo) {
             // prod[0:16lo, :] += Lfac[16lo:16cur, 0:16lo]^T . E[16lo:16cur, :]
             prof_begin_launch(stream, PROF_GEMM,
                               (double)(16 * lo) * a.n * (16 * (cur - lo)) * 2.0);
-            int rc = launch_gemm_tn_acc_f32(16 * lo, a.n, 16 * (cur - lo),
-                                            a.Lfac + (size_t)16 * lo * a.k, a.k,
-                                            a.E + (size_t)16 * lo * a.n, a.n,
-                                            a.prod, a.n, stream);
+            rc = launch_gemm_tn_acc_f32(16 * lo, a.n, 16 * (cur - lo),
+                                        a.Lfac + (size_t)16 * lo * a.k, a.k,
+                                        a.E + (size_t)16 * lo * a.n, a.n,
+                                        a.prod, a.n, stream);
             prof_end_launch(stream);
             if (rc) return rc;
         }

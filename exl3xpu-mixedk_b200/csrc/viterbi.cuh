@@ -52,7 +52,14 @@ struct Geo {
     static constexpr int BPTB = NOUT * BPE / 8;       // backpointer bytes / thread / step
     static constexpr int BP_ROW = kVT * BPTB;         // backpointer bytes per step
     static constexpr int TB_ROWS = kTbBytes / BP_ROW; // rows per traceback chunk
-    static constexpr bool TRANSPOSED = K >= 5;        // best-array smem layout
+    // best-array smem layout: transposed for K >= 5 (16-byte loads of a
+    // butterfly's inputs); natural for K <= 4, where a transposed layout turns
+    // every output store into a bank conflict (a warp's lanes write rows 8
+    // apart in one column)
+    static constexpr bool TRANSPOSED = K >= 5;
+    // transposed row stride: NC floats, padded by 4 when a row is < 32 words
+    // so that four consecutive butterflies start in different bank groups
+    static constexpr int ROW = (NC < 32) ? NC + 4 : NC;
     static constexpr int NCH = (NJ >= 4) ? 1 : 4 / NJ;  // partial min chains
 
     // output index j of thread t's e-th output
@@ -65,9 +72,9 @@ struct Geo {
         return WHOLE ? t + kVT * b : t / TPB;
     }
     // shared-memory address of best[idx].  Transposed for K >= 5 so that a
-    // butterfly's 2^K inputs are contiguous (vector loads).
+    // butterfly's 2^K inputs are contiguous (16-byte vector loads).
     static __device__ __forceinline__ int baddr(int idx) {
-        if (TRANSPOSED) return (idx & (P - 1)) * NC + (idx >> LOGP);
+        if (TRANSPOSED) return (idx & (P - 1)) * ROW + (idx >> LOGP);
         return idx;
     }
     // backpointer of output j inside one staged row
@@ -90,7 +97,8 @@ struct Geo {
 // Shared-memory layout of a tile CTA (dynamic shared memory).
 template <int K>
 struct VitSmem {
-    static constexpr int B_BYTES = Geo<K>::SPRE * 4;
+    static constexpr int B_BYTES =
+        (Geo<K>::TRANSPOSED ? Geo<K>::P * Geo<K>::ROW : Geo<K>::SPRE) * 4;
     static constexpr int OFF_B0 = 0;
     static constexpr int OFF_B1 = B_BYTES;
     static constexpr int OFF_X = 2 * B_BYTES;          // 256 fp32 targets
@@ -160,18 +168,70 @@ __device__ __forceinline__ float vit_d(const __half2 (&f2)[64], int r, float x) 
 }
 
 // Compare-and-update of one add-compare-select: if c < best then best = c and
-// the bit field [pos, pos+len) of `idx` becomes w.  Strict < keeps the first
-// (lowest) w on ties, like torch.min.  Predicated so that, with w / pos / len
-// compile-time constants, it issues as setp + 2 predicated ops.
-__device__ __forceinline__ void acs_update(float& best, uint32_t& idx, float c,
-                                           uint32_t clear_mask, uint32_t setv) {
+// idx = W.  Strict < keeps the first (lowest) predecessor on ties, like
+// torch.min.  W is an immediate, so this issues as setp + two predicated moves.
+template <int W>
+__device__ __forceinline__ void acs_update(float& best, int& idx, float c) {
     asm("{\n\t.reg .pred p;\n\t"
         "setp.lt.f32 p, %2, %0;\n\t"
         "@p mov.f32 %0, %2;\n\t"
-        "@p and.b32 %1, %1, %3;\n\t"
-        "@p or.b32 %1, %1, %4;\n\t}"
+        "@p mov.b32 %1, %3;\n\t}"
         : "+f"(best), "+r"(idx)
-        : "f"(c), "r"(clear_mask), "r"(setv));
+        : "f"(c), "n"(W));
+}
+
+template <int K, int W, int NJ, int NCH>
+struct AcsRow {
+    // one predecessor w = W for all NJ outputs of butterfly slice b
+    static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x, float bw,
+                                               int b, float (&best)[NJ][NCH],
+                                               int (&bi)[NJ][NCH]) {
+        constexpr int ch = W % NCH;
+#pragma unroll
+        for (int u = 0; u < NJ; ++u) {
+            const float d = vit_d<K>(f2, (b * NJ + u) * (1 << K) + W, x);
+            const float c = __fadd_rn(__fmul_rn(d, d), bw);
+            if (W < NCH) {
+                best[u][ch] = c;
+                bi[u][ch] = W;
+            } else {
+                acs_update<W>(best[u][ch], bi[u][ch], c);
+            }
+        }
+    }
+};
+
+template <int K, int W, int NJ, int NCH>
+struct AcsLoop {
+    static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x,
+                                               const float (&bin)[1 << K], int b,
+                                               float (&best)[NJ][NCH], int (&bi)[NJ][NCH]) {
+        AcsRow<K, W, NJ, NCH>::run(f2, x, bin[W], b, best, bi);
+        AcsLoop<K, W + 1, NJ, NCH>::run(f2, x, bin, b, best, bi);
+    }
+};
+template <int K, int NJ, int NCH>
+struct AcsLoop<K, (1 << K), NJ, NCH> {
+    static __device__ __forceinline__ void run(const __half2 (&)[64], float,
+                                               const float (&)[1 << K], int,
+                                               float (&)[NJ][NCH], int (&)[NJ][NCH]) {}
+};
+
+// Butterfly inputs best_i[m + w*P], w < 2^K, into registers.
+template <int K>
+__device__ __forceinline__ void vit_load_bin(const float* __restrict__ Bc, int m,
+                                             float (&bin)[1 << K]) {
+    using G = Geo<K>;
+    if (G::TRANSPOSED) {
+#pragma unroll
+        for (int w4 = 0; w4 < G::NC; w4 += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(&Bc[G::baddr(m) + w4]);
+            bin[w4] = q.x; bin[w4 + 1] = q.y; bin[w4 + 2] = q.z; bin[w4 + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int w = 0; w < G::NC; ++w) bin[w] = Bc[m + w * G::P];
+    }
 }
 
 // One trellis step: best_{i+1} = min-plus over this thread's states using
@@ -183,64 +243,29 @@ __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
                                              float* __restrict__ Bn, int t) {
     using G = Geo<K>;
     constexpr int NCH = G::NCH;
-    constexpr int BPE = G::BPE;
-    constexpr uint32_t FM = (1u << BPE) - 1u;
+    constexpr int NJ = G::NJ;
     uint64_t bits = 0;
 #pragma unroll
     for (int b = 0; b < G::NB; ++b) {
         const int m = G::bfly(t, b);
-        float best[G::NJ][NCH];
-        uint32_t pk[NCH];             // packed argmins of this butterfly slice
+        float best[NJ][NCH];
+        int bi[NJ][NCH];
+        float bin[1 << K];
+        vit_load_bin<K>(Bc, m, bin);
+        AcsLoop<K, 0, NJ, NCH>::run(f2, x, bin, b, best, bi);
 #pragma unroll
-        for (int ch = 0; ch < NCH; ++ch) pk[ch] = 0u;
-#pragma unroll
-        for (int w4 = 0; w4 < G::NC; w4 += 4) {
-            float bin[4];
-            if (G::TRANSPOSED) {
-                const float4 q = *reinterpret_cast<const float4*>(&Bc[m * G::NC + w4]);
-                bin[0] = q.x; bin[1] = q.y; bin[2] = q.z; bin[3] = q.w;
-            } else {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) bin[q] = Bc[m + (w4 + q) * G::P];
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int w = w4 + q;
-                const int ch = w % NCH;
-#pragma unroll
-                for (int u = 0; u < G::NJ; ++u) {
-                    const float d = vit_d<K>(f2, (b * G::NJ + u) * G::NC + w, x);
-                    const float c = __fadd_rn(__fmul_rn(d, d), bin[q]);
-                    const int pos = u * BPE;
-                    if (w < NCH) {
-                        best[u][ch] = c;
-                        if (w) pk[ch] |= (uint32_t)w << pos;
-                    } else {
-                        acs_update(best[u][ch], pk[ch], c, ~(FM << pos),
-                                   (uint32_t)w << pos);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < G::NJ; ++u) {
-            const int pos = u * BPE;
+        for (int u = 0; u < NJ; ++u) {
             float bv = best[u][0];
-            uint32_t bx = (pk[0] >> pos) & FM;
+            int bx = bi[u][0];
 #pragma unroll
             for (int ch = 1; ch < NCH; ++ch) {   // (value, index) lexicographic
-                const uint32_t ix = (pk[ch] >> pos) & FM;
-                const bool take = best[u][ch] < bv || (best[u][ch] == bv && ix < bx);
+                const bool take = best[u][ch] < bv || (best[u][ch] == bv && bi[u][ch] < bx);
                 bv = take ? best[u][ch] : bv;
-                bx = take ? ix : bx;
+                bx = take ? bi[u][ch] : bx;
             }
-            const int e = b * G::NJ + u;
+            const int e = b * NJ + u;
             Bn[G::baddr(G::out_j(t, e))] = bv;
-            if (NCH == 1) {
-                if (u == 0) bits |= static_cast<uint64_t>(pk[0]) << (b * G::NJ * BPE);
-            } else {
-                bits |= static_cast<uint64_t>(bx) << (e * BPE);
-            }
+            bits |= static_cast<uint64_t>(bx) << (e * G::BPE);
         }
     }
     return bits;

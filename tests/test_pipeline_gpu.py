@@ -230,3 +230,25 @@ def test_hessian_fallback_and_nonfinite(xq):
     Hn[3, 5] = float("nan")
     with pytest.raises(RuntimeError):
         xq.quantize_linear(W, Hn, K=3)
+
+
+def test_sweep_with_more_tiles_than_resident_ctas(xq, oracle, mul1_lut):
+    """Buffer launches of 8 x 160 tiles exceed the CTAs a B200 keeps resident
+    (one per SM): the dependency-ordered tile scheduling must still finish and
+    encode every tile exactly like the CPU oracle on the same targets."""
+    from exl3b import api
+    k, n, K = 256, 2560, 4
+    W, H = _ldlq_problem(k, 128, 41)
+    dev = torch.device("cuda", 0)
+    Lfac = api._damped_lfac(H[:k, :k] if H.shape[0] >= k else H, xq.sign_vec(k, 5).half(),
+                            0.01, dev)
+    Wq = torch.randn(k, n, generator=torch.Generator().manual_seed(8)).to(dev)
+    hatW, trl, st, X = api._sweep(Wq, Lfac, [K], [n], "exl3_mul1", 128, 0, 128,
+                                  want_states=True, want_x=True)
+    Xh, sth = X.cpu().numpy(), st.cpu().numpy()
+    for i in (0, 7, 8, 15):                    # first / last block of each buffer
+        ref = oracle.tailbite(Xh[i][::8], mul1_lut, K, pivot=128, margin=0, nthreads=NTH)
+        assert np.array_equal(ref, sth[i][::8]), f"k-block {i}"
+    lut = xq.get_lut("exl3_mul1").to(dev)
+    dec = xq.decode_trellis(trl[0], lut, K, k, n)
+    assert torch.equal(dec, hatW)
