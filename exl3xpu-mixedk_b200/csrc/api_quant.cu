@@ -356,9 +356,40 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
                   "column %d, column progress %d; slots held %d of %d, first holders "
                   "%d %d %d %d %d %d %d %d",
                   err[0] == 1 ? "no free backpointer slot" :
-                  err[0] == 2 ? "dependency wait timed out" : "aborted", err[1], err[2],
+                  err[0] == 2 ? "dependency wait timed out" :
+                  err[0] == 4 ? "feedback GEMM barrier timed out" : "aborted", err[1], err[2],
                   err[3], err[4], err[13], a.nslots, err[5], err[6], err[7], err[8], err[9],
                   err[10], err[11], err[12]);
+        return RC_DEVICE_ERROR;
+    }
+    return RC_OK;
+}
+
+int exl3b_feedback_gemm(int M, int N, int K, const float* dA_T, int lda, const float* dB,
+                        int ldb, float* dC, int ldc, void* ws, size_t ws_bytes, void* stream) {
+    if (M < 0 || N < 0 || K < 0 || lda < M || ldb < N || ldc < N) {
+        set_error("feedback GEMM dims M=%d N=%d K=%d lda=%d ldb=%d ldc=%d", M, N, K, lda, ldb, ldc);
+        return RC_BAD_REQUEST;
+    }
+    if (!ws || ws_bytes < 256 || ((uintptr_t)ws & 255)) {
+        set_error("feedback GEMM needs a 256-byte status workspace");
+        return RC_WORKSPACE;
+    }
+    DeviceState* st;
+    if (need_device(&st)) return RC_NO_DEVICE;
+    cudaStream_t s = S(stream);
+    int* err = static_cast<int*>(ws);
+    if (check_cuda(cudaMemsetAsync(err, 0, sizeof(int), s), "memset gemm status"))
+        return RC_DEVICE_ERROR;
+    int rc = launch_gemm_tn_acc_tc(M, N, K, dA_T, lda, dB, ldb, dC, ldc, err, s);
+    if (rc) return rc;
+    int h = 0;
+    if (check_cuda(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, s),
+                   "read gemm status") ||
+        check_cuda(cudaStreamSynchronize(s), "gemm sync"))
+        return RC_DEVICE_ERROR;
+    if (h) {
+        set_error("feedback GEMM: a barrier wait timed out");
         return RC_DEVICE_ERROR;
     }
     return RC_OK;

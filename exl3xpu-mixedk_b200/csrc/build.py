@@ -60,7 +60,7 @@ def build(verbose_ptxas: bool = False, jobs: int = 8) -> str:
         print(logs)
     newest = max(os.path.getmtime(o) for o in objs)
     if not os.path.exists(OUT) or os.path.getmtime(OUT) < newest:
-        cmd = [NVCC, *ARCH, "-shared", "-o", OUT, *objs, "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", OUT, *objs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -104,6 +104,8 @@ int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream
 int u_to_gram_f64(const float* U, int n, double* Ud, double* Ui, double* G, cudaStream_t stream);
 int launch_gemm_tn_acc_f32(int M, int N, int K, const float* A_T, int lda,
                            const float* B, int ldb, float* C, int ldc, cudaStream_t stream);
+int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const float* B,
+                          int ldb, float* C, int ldc, int* err, cudaStream_t stream);
 
 // ------------------------------------------------------------ LDLQ sweep
 struct SweepArgs {

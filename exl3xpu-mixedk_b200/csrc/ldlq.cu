@@ -18,7 +18,8 @@
 // resident and finishes: no deadlock, and no wave quantisation (320 column
 // tiles on 148 SMs would otherwise leave the third wave 84% idle).  The wait is
 // bounded; on time-out the CTA sets an error word and returns.  After a
-// buffer, prod[:16lo] += Lfac[buf, :16lo]^T E[buf].  Columns never interact
+// buffer, prod[:16lo] += Lfac[buf, :16lo]^T E[buf] on tcgen05 tensor cores
+// (gemm_tc.cu, 3xTF32, TMA-fed).  Columns never interact
 // (Lfac couples rows only), so each CTA owns one column tile of one k-block:
 //   WXWX = (Wq + Lfac[later, blk]^T . E[later]) + prod     (quantize.py:676-682)
 //   x[t] = WXWX[perm[t]]                                   (:684-686)
@@ -379,10 +380,10 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
             // prod[0:16lo, :] += Lfac[16lo:16cur, 0:16lo]^T . E[16lo:16cur, :]
             prof_begin_launch(stream, PROF_GEMM,
                               (double)(16 * lo) * a.n * (16 * (cur - lo)) * 2.0);
-            rc = launch_gemm_tn_acc_f32(16 * lo, a.n, 16 * (cur - lo),
-                                        a.Lfac + (size_t)16 * lo * a.k, a.k,
-                                        a.E + (size_t)16 * lo * a.n, a.n,
-                                        a.prod, a.n, stream);
+            rc = launch_gemm_tn_acc_tc(16 * lo, a.n, 16 * (cur - lo),
+                                       a.Lfac + (size_t)16 * lo * a.k, a.k,
+                                       a.E + (size_t)16 * lo * a.n, a.n,
+                                       a.prod, a.n, a.err, stream);
             prof_end_launch(stream);
             if (rc) return rc;
         }

@@ -235,6 +235,15 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
                      int32_t* dStates, float* dXout, int block_lo, int block_hi,
                      void* ws, size_t ws_bytes, void* stream);
 
+/* LDLQ feedback-cache update (quantize.py:742-744) on tcgen05 tensor cores:
+ *   C[M][N] += A_T^T . B,   A_T [K][M] (row pitch lda), B [K][N] (pitch ldb)
+ * 3xTF32 (fp32-grade) products, TMA-fed, fp32 accumulation.  Pointers 16-byte
+ * aligned, lda / ldb multiples of 4.  ws: >= 256 bytes of device scratch for a
+ * status word.  Synchronises `stream`. */
+int exl3b_feedback_gemm(int M, int N, int K, const float* dA_T, int lda, const float* dB,
+                        int ldb, float* dC, int ldc, void* ws, size_t ws_bytes,
+                        void* stream);
+
 /* Bitstream (quantize.py:360-415): pack int32 states [ntiles][256] into
  * int16 [ntiles][16K]; unpack back to full 16-bit states; decode a trellis
  * [tk][tn][16K] to W_inner fp32 [16 tk][16 tn] through code `code`. */

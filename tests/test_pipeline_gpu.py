@@ -252,3 +252,24 @@ def test_sweep_with_more_tiles_than_resident_ctas(xq, oracle, mul1_lut):
     lut = xq.get_lut("exl3_mul1").to(dev)
     dec = xq.decode_trellis(trl[0], lut, K, k, n)
     assert torch.equal(dec, hatW)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 200, 128), (128, 128, 32), (5104, 5120, 128),
+                                   (64, 1024, 80)])
+def test_feedback_gemm_tcgen05(M, N, K):
+    """The tensor-core feedback update C += A_T^T B (3xTF32) against an fp64
+    torch reference: fp32-grade accuracy, partial tiles, K not a multiple of
+    32 (zero-filled TMA boxes)."""
+    from exl3b import native
+    gen = torch.Generator(device="cuda").manual_seed(M + N + K)
+    lda, ldb = M + 20, N + 12
+    A = torch.randn(K, lda, device="cuda", generator=gen)
+    B = torch.randn(K, ldb, device="cuda", generator=gen)
+    C = torch.randn(M, N, device="cuda", generator=gen)
+    ref = C.double() + A[:, :M].double().t() @ B[:, :N].double()
+    ws = torch.empty(256, dtype=torch.uint8, device="cuda")
+    native.call("exl3b_feedback_gemm", M, N, K, A.data_ptr(), lda, B.data_ptr(), ldb,
+                C.data_ptr(), N, ws.data_ptr(), 256, None)
+    err = (C.double() - ref).abs().max().item()
+    scale = (A[:, :M].double().abs().t() @ B[:, :N].double().abs()).max().item()
+    assert err <= 2e-6 * scale, (err, scale)
