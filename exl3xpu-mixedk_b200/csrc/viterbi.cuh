@@ -20,7 +20,7 @@
 //    512 threads owns 128 fixed states (whole butterflies for K <= 3, a slice of
 //    one butterfly for K >= 4) and holds their decode values in 64 packed-fp16
 //    registers for the whole kernel (EXL3 decode values are exact in fp16), so
-//    one add-compare-select is: unpack, fsub, fmul, fadd, compare, 2 selects --
+//    one add-compare-select is: mixed fp16-fp32 sub, fmul, fadd, compare, 2 selects --
 //    no shared-memory gather on the inner loop.
 //  * Backpointers: each thread packs its outputs' K-bit argmins into one
 //    8/16/32/64-bit word per step and stores it coalesced to global scratch
@@ -144,21 +144,23 @@ __device__ __forceinline__ void vit_load_f2tab(__half2 (&f2)[64],
 }
 
 // d = fl(f - x) with f the low (HI=false) or high half of a packed pair.  The
-// unpack and the subtraction sit in one asm block that consumes x, so the
-// compiler cannot hoist 128 unpacked decode values out of the step loop
+// sm_100 mixed-precision subtract takes the fp16 half directly (exact widening,
+// one fp32 rounding), so this is one instruction and bit-identical to
+// fl(float(f) - x).  Keeping it in an asm block that consumes x also stops the
+// compiler from hoisting 128 unpacked decode values out of the step loop
 // (which would need 128 extra registers).
 template <bool HI>
 __device__ __forceinline__ float sub_f16(__half2 h2, float x) {
     const uint32_t r = *reinterpret_cast<const uint32_t*>(&h2);
     float d;
     if (HI)
-        asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 f;\n\t"
-            "mov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 f, hi;\n\t"
-            "sub.rn.f32 %0, f, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
+        asm("{\n\t.reg .b16 lo, hi;\n\t"
+            "mov.b32 {lo, hi}, %1;\n\t"
+            "sub.rn.f32.f16 %0, hi, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
     else
-        asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 f;\n\t"
-            "mov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 f, lo;\n\t"
-            "sub.rn.f32 %0, f, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
+        asm("{\n\t.reg .b16 lo, hi;\n\t"
+            "mov.b32 {lo, hi}, %1;\n\t"
+            "sub.rn.f32.f16 %0, lo, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
     return d;
 }
 
@@ -180,7 +182,10 @@ __device__ __forceinline__ void acs_update(float& best, int& idx, float c) {
         : "f"(c), "n"(W));
 }
 
-template <int K, int W, int NJ, int NCH>
+// TRACK = false: the step's backpointers are never read (pass-1 steps before
+// the traceback stop), so only the minimum is kept: one min instead of a
+// compare and two selects.  The minimum value is the same either way.
+template <int K, int W, int NJ, int NCH, bool TRACK>
 struct AcsRow {
     // one predecessor w = W for all NJ outputs of butterfly slice b
     static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x, float bw,
@@ -193,25 +198,27 @@ struct AcsRow {
             const float c = __fadd_rn(__fmul_rn(d, d), bw);
             if (W < NCH) {
                 best[u][ch] = c;
-                bi[u][ch] = W;
-            } else {
+                if (TRACK) bi[u][ch] = W;
+            } else if (TRACK) {
                 acs_update<W>(best[u][ch], bi[u][ch], c);
+            } else {
+                best[u][ch] = fminf(best[u][ch], c);
             }
         }
     }
 };
 
-template <int K, int W, int NJ, int NCH>
+template <int K, int W, int NJ, int NCH, bool TRACK>
 struct AcsLoop {
     static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x,
                                                const float (&bin)[1 << K], int b,
                                                float (&best)[NJ][NCH], int (&bi)[NJ][NCH]) {
-        AcsRow<K, W, NJ, NCH>::run(f2, x, bin[W], b, best, bi);
-        AcsLoop<K, W + 1, NJ, NCH>::run(f2, x, bin, b, best, bi);
+        AcsRow<K, W, NJ, NCH, TRACK>::run(f2, x, bin[W], b, best, bi);
+        AcsLoop<K, W + 1, NJ, NCH, TRACK>::run(f2, x, bin, b, best, bi);
     }
 };
-template <int K, int NJ, int NCH>
-struct AcsLoop<K, (1 << K), NJ, NCH> {
+template <int K, int NJ, int NCH, bool TRACK>
+struct AcsLoop<K, (1 << K), NJ, NCH, TRACK> {
     static __device__ __forceinline__ void run(const __half2 (&)[64], float,
                                                const float (&)[1 << K], int,
                                                float (&)[NJ][NCH], int (&)[NJ][NCH]) {}
@@ -236,8 +243,8 @@ __device__ __forceinline__ void vit_load_bin(const float* __restrict__ Bc, int m
 
 // One trellis step: best_{i+1} = min-plus over this thread's states using
 // best_i (Bc) and target x; writes best_{i+1} (Bn), returns packed argmins
-// (output e's argmin w in bits [e*BPE, e*BPE + BPE)).
-template <int K>
+// (output e's argmin w in bits [e*BPE, e*BPE + BPE)); 0 when !TRACK.
+template <int K, bool TRACK = true>
 __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
                                              const float* __restrict__ Bc,
                                              float* __restrict__ Bn, int t) {
@@ -252,20 +259,26 @@ __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
         int bi[NJ][NCH];
         float bin[1 << K];
         vit_load_bin<K>(Bc, m, bin);
-        AcsLoop<K, 0, NJ, NCH>::run(f2, x, bin, b, best, bi);
+        AcsLoop<K, 0, NJ, NCH, TRACK>::run(f2, x, bin, b, best, bi);
 #pragma unroll
         for (int u = 0; u < NJ; ++u) {
             float bv = best[u][0];
-            int bx = bi[u][0];
-#pragma unroll
-            for (int ch = 1; ch < NCH; ++ch) {   // (value, index) lexicographic
-                const bool take = best[u][ch] < bv || (best[u][ch] == bv && bi[u][ch] < bx);
-                bv = take ? best[u][ch] : bv;
-                bx = take ? bi[u][ch] : bx;
-            }
             const int e = b * NJ + u;
+            if (TRACK) {
+                int bx = bi[u][0];
+#pragma unroll
+                for (int ch = 1; ch < NCH; ++ch) {   // (value, index) lexicographic
+                    const bool take =
+                        best[u][ch] < bv || (best[u][ch] == bv && bi[u][ch] < bx);
+                    bv = take ? best[u][ch] : bv;
+                    bx = take ? bi[u][ch] : bx;
+                }
+                bits |= static_cast<uint64_t>(bx) << (e * G::BPE);
+            } else {
+#pragma unroll
+                for (int ch = 1; ch < NCH; ++ch) bv = fminf(bv, best[u][ch]);
+            }
             Bn[G::baddr(G::out_j(t, e))] = bv;
-            bits |= static_cast<uint64_t>(bx) << (e * G::BPE);
         }
     }
     return bits;
@@ -312,10 +325,19 @@ __device__ __forceinline__ int vit_pass(const __half2 (&f2)[64], char* smem, int
         Bc[G::baddr(idx)] = (overlap < 0 || idx == overlap) ? 0.0f : INF;
     __syncthreads();
 
-    for (int i = 0; i < nsteps - 1; ++i) {
+    // steps whose backpointer row lies at or before `stop` are never traced
+    // back through: minimum only
+    const int nfree = min(max(stop, 0), nsteps - 1);
+    for (int i = 0; i < nfree; ++i) {
+        const float x = xs[(i - rol) & 255];
+        vit_step<K, false>(f2, x, Bc, Bn, t);
+        float* tmp = Bc; Bc = Bn; Bn = tmp;
+        __syncthreads();
+    }
+    for (int i = nfree; i < nsteps - 1; ++i) {
         const float x = xs[(i - rol) & 255];
         const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t);
-        if (i + 1 > stop) vit_store_bits<K>(bp + (size_t)(i + 1) * G::BP_ROW, bits, t);
+        vit_store_bits<K>(bp + (size_t)(i + 1) * G::BP_ROW, bits, t);
         float* tmp = Bc; Bc = Bn; Bn = tmp;
         __syncthreads();
     }
