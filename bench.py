@@ -17,6 +17,14 @@ mul1, quantize_linear defaults: pivot 128, margin 0), packing and W_hat.
           rank, no collective on the data path): weak scaling
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config c2|c3|c4] [--K k]
+
+The default line is configuration 2 (the driver's bench line).  --config c3
+(fused q/k/v module, K = [5, 7, 7], one shared Hessian) and --config c4
+(17408 -> 5120 down projection at --K) print the same line for those
+workloads.  "kernels" adds each device stage's roofline: the fused tile kernel
+(ALU lanes), the tcgen05 feedback GEMM (useful FLOP vs the TF32 tensor rate),
+the Hadamard rotations (HBM bytes) and the block LDL (fp32 FMA rate).
 
 --impl reference times the reference algorithm's CPU implementation (the C/numpy
 restatement under oracle/; the reference itself is Python and does not travel)
@@ -183,6 +191,101 @@ def _cpu_problem():
     return Wq, Lfac.astype(np.float32), lut
 
 
+def _workload(args, rank, dev):
+    """(label, metric, weights, device inputs, step(inputs, out_device))."""
+    from exl3b import api, synth
+    if args.config == "c3":
+        Ws, H, Ks = synth.config3(device=dev, seed_offset=100 * rank)
+        label = ("config 3: fused q/k/v module, q 5120->6144, k/v 5120->1024 bf16 "
+                 "~N(0,0.02^2) + outliers, one shared H (4096 heavy-tailed rows), "
+                 "K = [5, 7, 7] mul1, one block-LDL + one sweep over the members")
+        metric = "trellis-encoded weights/s (Viterbi+LDLQ) at K=[5,7,7]"
+
+        def step(inp, od):
+            return api.quantize_linear_fused(inp[0], inp[1], Ks=Ks, device=dev, out_device=od)
+        return label, metric, sum(W.numel() for W in Ws), [Ws, H], step, \
+            {"k": 5120, "n": [6144, 1024, 1024], "K": Ks}
+    if args.config == "c4":
+        W, H = synth.config4(device=dev, seed_w=7 + 100 * rank, seed_h=8 + 100 * rank)
+        K = args.K
+        label = (f"config 4: MLP down projection 17408->5120 bf16 ~N(0,0.015^2) + outliers, "
+                 f"H of dim 17408 (4096 heavy-tailed rows), K={K} mul1, pivot 128, margin 0")
+        metric = f"trellis-encoded weights/s (Viterbi+LDLQ) at K={K}"
+
+        def step(inp, od):
+            return api.quantize_linear(inp[0], inp[1], K=K, device=dev, out_device=od)
+        return label, metric, W.numel(), [W, H], step, {"k": 17408, "n": 5120, "K": K}
+    if args.dim == DIM:
+        W, H = synth.config2(seed_w=1 + 100 * rank, seed_h=2 + 100 * rank, device=dev)
+        label = WORKLOAD
+    else:
+        W = synth.weight(args.dim, args.dim, 0.02, 1 + 100 * rank, dev)
+        H = synth.hessian(args.dim, 2 + 100 * rank, dev)
+        label = f"{args.dim}x{args.dim} profiling case (not a bench line)"
+
+    def step(inp, od):
+        return api.quantize_linear(inp[0], inp[1], K=K_BITS, device=dev, out_device=od)
+    return label, METRIC, W.numel(), [W, H], step, {"k": args.dim, "n": args.dim, "K": K_BITS}
+
+
+def _to_host(inp):
+    if isinstance(inp, list):
+        return [_to_host(x) for x in inp]
+    return inp.cpu().pin_memory()
+
+
+def _nbytes(x):
+    if isinstance(x, (list, tuple)):
+        return sum(_nbytes(y) for y in x)
+    return x.numel() * x.element_size()
+
+
+def _result_bytes(r):
+    if isinstance(r, list):
+        return sum(_result_bytes(x) for x in r)
+    return sum(r[k].numel() * r[k].element_size() for k in ("W_hat", "trellis", "suh", "svh"))
+
+
+def _prof(L, kind):
+    import ctypes
+    from exl3b import native
+    ms, n, u = ctypes.c_double(0.0), ctypes.c_longlong(0), ctypes.c_double(0.0)
+    native.check("exl3b_profile_end",
+                 L.exl3b_profile_end(kind, ctypes.byref(ms), ctypes.byref(n), ctypes.byref(u)))
+    return ms.value, n.value, u.value
+
+
+def _kernels(L, steps, step_ms, sms, peaks):
+    """Per-stage roofline from the library's per-launch events (kinds 0, 1, 3, 4)."""
+    mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    src = "MEASURED_PEAKS.json" if peaks else "fallback"
+    out = {}
+    specs = [
+        (0, "ldlq_tile", "alu", "Gop/s", lambda u: u * OPS_PER_WEIGHT / 1e9,
+         sms * 128 * mhz * 1e6 / 1e9,
+         f"{sms} SMs x 128 lanes x {mhz:.0f} MHz; 2 ops per add-compare-select"),
+        (1, "feedback_gemm_tcgen05", "tensor", "TFLOP/s", lambda u: u / 1e12, bf16 / 2.0,
+         f"TF32 dense = bf16 dense / 2 of {src} (useful FLOP; 3xTF32 issues 3 MMAs per "
+         "useful product, so frac <= 1/3)"),
+        (3, "hadamard_rotation", "hbm", "GB/s", lambda u: u / 1e9, hbm,
+         f"HBM copy bandwidth of {src} (algorithmic bytes: read input + write output once)"),
+        (4, "block_ldl", "fp32", "TFLOP/s", lambda u: u / 1e12, sms * 256 * mhz * 1e6 / 1e12,
+         f"{sms} SMs x 128 FMA lanes x 2 x {mhz:.0f} MHz; k^3/3 FLOP"),
+    ]
+    for kind, name, bound, unit, conv, peak, note in specs:
+        ms, n, u = _prof(L, kind)
+        if n == 0:
+            continue
+        ach = conv(u) / (ms / 1e3) if ms > 0 else None
+        out[name] = {"bound": bound, "ms_per_step": ms / steps, "launches_per_step": n / steps,
+                     "share_of_step": (ms / steps) / step_ms if step_ms else None,
+                     "achieved": ach, "peak": peak, "unit": unit,
+                     "frac": (ach / peak) if ach is not None else None, "peak_source": note}
+    return out
+
+
 def run_reference(args, rank):
     if rank != 0:
         return 0
@@ -217,6 +320,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4"],
+                    help="workload: c2 (default bench line), c3 fused mixed-K qkv, c4 at --K")
+    ap.add_argument("--K", type=int, default=4, help="bits per weight for --config c4")
     ap.add_argument("--dim", type=int, default=DIM,
                     help="projection size (default 5120 = config 2; smaller sizes are "
                          "for profiler captures, not bench lines)")
@@ -230,7 +336,7 @@ def main():
     import torch
     import torch.distributed as dist
     from datetime import timedelta
-    from exl3b import api, native, synth
+    from exl3b import native
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -239,15 +345,11 @@ def main():
                                 device_id=dev)
     L = native.lib()
 
-    if args.dim == DIM:
-        W, H = synth.config2(seed_w=1 + 100 * rank, seed_h=2 + 100 * rank, device=dev)
-    else:
-        W = synth.weight(args.dim, args.dim, 0.02, 1 + 100 * rank, dev)
-        H = synth.hessian(args.dim, 2 + 100 * rank, dev)
+    label, metric, weights, inputs, run_step, shape = _workload(args, rank, dev)
     torch.cuda.synchronize()
 
     def step():
-        return api.quantize_linear(W, H, K=K_BITS, device=dev, out_device=dev)
+        return run_step(inputs, dev)
 
     def barrier():
         if world > 1:
@@ -272,21 +374,17 @@ def main():
         r = step()
     e1.record(s)
     barrier()
-    import ctypes
-    ms_tile = ctypes.c_double(0.0)
-    n_tile = ctypes.c_longlong(0)
-    u_tile = ctypes.c_double(0.0)
-    native.check("exl3b_profile_end",
-                 L.exl3b_profile_end(0, ctypes.byref(ms_tile), ctypes.byref(n_tile),
-                                     ctypes.byref(u_tile)))
-    launches = (L.exl3b_launch_count() - n0) // args.steps
     clocks = sampler.stop(set(range(max(world, 1)))) if sampler else None
+    launches = (L.exl3b_launch_count() - n0) // args.steps
     ms = e0.elapsed_time(e1) / args.steps
+    peaks = _measured_peaks()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    kernels = _kernels(L, args.steps, ms, sms, peaks)
+    ms_tile, n_tile, u_tile = _prof(L, 0)
     t_max = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms = float(t_max.item())
-    weights = args.dim * args.dim
     value = world * weights / (ms / 1e3)
 
     # ---- e2e: public API from pinned host buffers, copies inside the step
@@ -294,33 +392,30 @@ def main():
     h2d = d2h = 0
     del r
     if not args.no_e2e:
-        W_h = W.cpu().pin_memory()
-        H_h = H.cpu().pin_memory()
-        api.quantize_linear(W_h, H_h, K=K_BITS, device=dev, out_device="cpu")
+        host = _to_host(inputs)
+        run_step(host, "cpu")
         barrier()
         e2 = torch.cuda.Event(enable_timing=True)
         e3 = torch.cuda.Event(enable_timing=True)
         e2.record(s)
         for _ in range(args.steps):
-            rr = api.quantize_linear(W_h, H_h, K=K_BITS, device=dev, out_device="cpu")
+            rr = run_step(host, "cpu")
         e3.record(s)
         barrier()
         ms_e2e = e2.elapsed_time(e3) / args.steps
-        h2d = W_h.numel() * W_h.element_size() + H_h.numel() * H_h.element_size()
-        d2h = sum(rr[k].numel() * rr[k].element_size()
-                  for k in ("W_hat", "trellis", "suh", "svh"))
+        h2d = _nbytes(host)
+        d2h = _result_bytes(rr)
+        del rr
     t2 = torch.tensor([ms_e2e], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     ms_e2e = float(t2.item())
 
     # ---- roofline of the dominant kernel (fused LDLQ tile kernel)
-    peaks = _measured_peaks()
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
     mhz = float(peaks.get("sm_max_mhz", 1965.0))
     peak_ops = sms * 128 * mhz * 1e6 / 1e9           # Gop/s
-    tile_ms_avg = ms_tile.value / max(n_tile.value, 1)
-    w_per_launch = u_tile.value / max(n_tile.value, 1)
+    tile_ms_avg = ms_tile / max(n_tile, 1)
+    w_per_launch = u_tile / max(n_tile, 1)
     achieved = w_per_launch * OPS_PER_WEIGHT / (tile_ms_avg / 1e3) / 1e9
     tpw = _profile_traffic()
     roofline = {
@@ -330,36 +425,40 @@ def main():
         "peak_source": f"{sms} SMs x 128 lanes x {mhz:.0f} MHz (sm_max_mhz of "
                        "MEASURED_PEAKS.json); 2 ops per add-compare-select",
         "ops_per_weight": OPS_PER_WEIGHT,
-        "launches_per_step": n_tile.value / args.steps,
+        "launches_per_step": n_tile / args.steps,
         "avg_launch_ms": tile_ms_avg,
-        "share_of_step": ms_tile.value / args.steps / ms if ms else None,
+        "share_of_step": ms_tile / args.steps / ms if ms else None,
         "traffic": (tpw * w_per_launch) if tpw else None,
         "traffic_unit": "bytes per launch",
     }
 
+    in_bytes = _nbytes(inputs)
+    config = {"workload": label, **shape,
+              "per_rank": "one independent problem per rank (seeds offset by 100 r)",
+              "l2": f"inputs larger than L2 ({in_bytes / 1e6:.0f} MB of W and H per step, "
+                    "plus the sweep's intermediates)",
+              "parallelism": f"{world} independent ranks"}
+    if args.config != "c2":
+        config["config"] = args.config
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "metric": metric, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD if args.dim == DIM else f"{args.dim}x{args.dim} "
-                   "profiling case (not a bench line)", "k": args.dim, "n": args.dim,
-                   "K": K_BITS,
-                   "per_rank": "one projection per rank (seed 1+100r / 2+100r)",
-                   "l2": "inputs larger than L2 (W 52 MB bf16 + H 105 MB fp32 per step, "
-                         "plus ~1 GB of intermediates)",
-                   "parallelism": f"{world} independent ranks"},
+        "config": config,
         "e2e": {"value": world * weights / (ms_e2e / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": ms_e2e},
         "gpu_launches": int(launches),
         "roofline": roofline,
+        "kernels": kernels,
         "clocks": clocks,
         "per_layer_s": ms / 1e3,
     }
     if world > 1:
         dist.barrier(device_ids=[local])
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.dim == DIM:
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.dim == DIM
+            and args.config == "c2"):
         Wq, Lfac, lut = _cpu_problem()
         times, nth = _cpu_sample(Wq, Lfac, lut, 2, warm=1)
         t = sum(times) / len(times)

@@ -22,6 +22,15 @@ int need_device(DeviceState** st) {
 
 bool dims128(int a, int b) { return a > 0 && b > 0 && a % 128 == 0 && b % 128 == 0; }
 
+// One two-sided rotation launch, recorded as PROF_ROTATE with its
+// algorithmic bytes (read input + write output once).
+int had2_profiled(const HadParams& p, cudaStream_t s, double bytes) {
+    prof_begin_launch(s, PROF_ROTATE, bytes);
+    const int rc = launch_had2(p, s);
+    prof_end_launch(s);
+    return rc;
+}
+
 }  // namespace
 
 extern "C" {
@@ -41,7 +50,7 @@ int exl3b_incoherence_fwd(const void* dW, int dtype, int m_out, int k_in,
     p.Y = dWi; p.ldy = m_out; p.trans_out = false;
     p.rows = k_in; p.cols = m_out; p.pre_scale = 1.0f;
     p.pre_r = d_row_mul; p.pre_c = d_col_mul; p.sumsq = d_sumsq_parts;
-    return launch_had2(p, S(stream));
+    return had2_profiled(p, S(stream), (double)m_out * k_in * ((dtype == 0 ? 4 : 2) + 4));
 }
 
 int exl3b_incoherence_inv(const float* dWi, int k, int n, const float* d_pre_scale,
@@ -58,7 +67,7 @@ int exl3b_incoherence_inv(const float* dWi, int k, int n, const float* d_pre_sca
     p.Y = dW; p.ldy = k; p.trans_out = true;
     p.rows = k; p.cols = n; p.pre_scale = 1.0f; p.pre_scale_dev = d_pre_scale;
     p.mid_r = d_su; p.post_c = d_sv;
-    return launch_had2(p, S(stream));
+    return had2_profiled(p, S(stream), (double)k * n * 8);
 }
 
 int exl3b_rotate_hessian(const float* dH, int k, const float* d_su, float* dG,
@@ -73,7 +82,7 @@ int exl3b_rotate_hessian(const float* dH, int k, const float* d_su, float* dG,
     memset(&p, 0, sizeof(p));
     p.X = dH; p.in_dtype = 0; p.ldx = k; p.Y = dG; p.ldy = k;
     p.rows = k; p.cols = k; p.pre_scale = 1.0f; p.pre_r = d_su; p.pre_c = d_su;
-    return launch_had2(p, S(stream));
+    return had2_profiled(p, S(stream), (double)k * k * 8);
 }
 
 int exl3b_damp_hessian(float* dG, int k, float percdamp, int* d_nonfinite, void* stream) {
@@ -206,10 +215,12 @@ int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
     int* status = reinterpret_cast<int*>(w + align256((size_t)(k / 16) * 256 * es));
     cudaStream_t s = S(stream);
     if (check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "memset status")) return RC_DEVICE_ERROR;
+    prof_begin_launch(s, PROF_LDL, (double)k * k * k / 3.0);
     int rc = f64 ? block_ldl<double>(static_cast<double*>(dA), k, dLfac, static_cast<double*>(dD),
                                      static_cast<double*>(dli), status, s)
                  : block_ldl<float>(static_cast<float*>(dA), k, dLfac, static_cast<float*>(dD),
                                     static_cast<float*>(dli), status, s);
+    prof_end_launch(s);
     if (rc) return rc;
     int h = 0;
     if (check_cuda(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, s),

@@ -4,7 +4,10 @@ directory.  nvcc cross-compiles; no GPU is needed.
 
     python exl3xpu-mixedk_b200/csrc/build.py [--verbose-ptxas] [-j N]
 
-Output: exl3xpu-mixedk_b200/exl3b/libexl3b200.so (in-tree, git-ignored).
+Outputs (in-tree, git-ignored):
+  exl3xpu-mixedk_b200/exl3b/libexl3b200.so   the C-ABI library
+  exl3xpu-mixedk_b200/exl3b/exl3b_vit        the serve / file-mode worker
+                                             (vit_serve.cpp, linked to the library)
 Objects are rebuilt only when a source or header is newer.
 """
 from __future__ import annotations
@@ -20,6 +23,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 REPO = os.path.dirname(PKG)
 OUT = os.path.join(PKG, "exl3b", "libexl3b200.so")
+WORKER = os.path.join(PKG, "exl3b", "exl3b_vit")
 BUILD = os.path.join(HERE, "_build")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -64,6 +68,15 @@ def build(verbose_ptxas: bool = False, jobs: int = 8) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    src = os.path.join(HERE, "vit_serve.cpp")
+    if not os.path.exists(WORKER) or os.path.getmtime(WORKER) < max(
+            os.path.getmtime(src), os.path.getmtime(OUT), _deps_mtime()):
+        cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-I",
+               os.path.join(REPO, "include"), src, "-o", WORKER,
+               "-L", os.path.dirname(OUT), "-l:libexl3b200.so", "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"worker build failed:\n{r.stdout}\n{r.stderr}")
     return OUT
 
 

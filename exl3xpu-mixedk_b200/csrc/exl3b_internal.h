@@ -29,7 +29,8 @@ struct DeviceState {
 // Kernel-launch accounting (exl3b_launch_count) and optional per-launch
 // CUDA-event timing of the dominant kernels (exl3b_profile_*).
 void note_launch(int n = 1);
-enum ProfKernel : int { PROF_TILE = 0, PROF_GEMM = 1, PROF_TAILBITE = 2, PROF_N = 3 };
+enum ProfKernel : int { PROF_TILE = 0, PROF_GEMM = 1, PROF_TAILBITE = 2, PROF_ROTATE = 3,
+                        PROF_LDL = 4, PROF_N = 5 };
 bool prof_on();
 void prof_begin_launch(cudaStream_t s, int kind, double units);
 void prof_end_launch(cudaStream_t s);

@@ -444,30 +444,70 @@ def quantize_linear(W: torch.Tensor, H_x: torch.Tensor | None, code: str = "exl3
     input Gram H_x [in, in] (None -> plain trellis encode of the incoherent
     weight).  Returns the reference's dict; tensors on `out_device`
     (CPU by default, like the reference)."""
+    return quantize_linear_fused(
+        [W], H_x, code=code, Ks=[K], L=L, V=V, percdamp=percdamp, su_seed=su_seed,
+        buf_cols=buf_cols, use_ldlq=use_ldlq, device=device, batch=batch, dtype=dtype,
+        margin=margin, compiled=compiled, progress=progress, backend=backend,
+        channel_scales=channel_scales, pivot=pivot, out_device=out_device,
+        keep_states=keep_states)[0]
+
+
+def quantize_linear_fused(Ws: list, H_x: torch.Tensor | None, code: str = "exl3_mul1",
+                          Ks: list | None = None, L: int = 16, V: int = 0,
+                          percdamp: float = 0.01, su_seed: int = 20261011,
+                          buf_cols: int = 128, use_ldlq: bool = True, device: str = "cpu",
+                          batch: int = 0, dtype: torch.dtype = torch.float32,
+                          margin: int = 0, compiled: bool = False, progress=None,
+                          backend: str = "cuda", channel_scales: bool = False,
+                          *, pivot: int | None = None, out_device="cpu",
+                          keep_states: bool = False) -> list:
+    """Members of one fused module (e.g. q/k/v: W_j [out_j, in], one shared
+    input Gram H_x) at per-member bit widths Ks[j] -- the mixed-K fused
+    module of serve/patches/0002-vllm-plugin-mixed-k.patch.  Returns one
+    quantize_linear dict per member, identical to quantize_linear(W_j, H_x,
+    K=Ks[j], ...) called member by member: the members share su (same seed
+    and k), hence the rotated Hessian and its block-LDL factor, which are
+    computed once; the LDLQ feedback couples rows only (quantize.py:680-682,
+    743-744), so one sweep over the members' columns side by side, each
+    column segment at its own K, gives each member's own result."""
     _check_backend(backend)
     _check_code(code, L, V)
-    _check_K(K)
-    m_out, k_in = W.shape
-    assert k_in % 128 == 0 and m_out % 128 == 0, (W.shape, "need k%128, n%128")
+    if Ks is None:
+        Ks = [4] * len(Ws)
+    if len(Ks) != len(Ws) or not Ws:
+        raise ValueError("need one K per member")
+    for K in Ks:
+        _check_K(K)
+    k_in = Ws[0].shape[1]
+    for W in Ws:
+        assert W.shape[1] == k_in, "fused members share the input dimension"
+        assert k_in % 128 == 0 and W.shape[0] % 128 == 0, (W.shape, "need k%128, n%128")
     dev = _cuda_device(device)
     _select(dev)
     lut = get_lut(code)
     lut_rms = _lut_rms(lut)
     suh = sign_vec(k_in, su_seed).half()
-    svh = sign_vec(m_out, su_seed + 1).half()
-    W_dev = W.detach().to(dev, non_blocking=True)
-    if W_dev.dtype not in DTYPE_IDS:
-        W_dev = W_dev.float()
-    W_dev = W_dev.contiguous()
 
-    if channel_scales:
-        from .incoherence import channel_scale_inner
-        Wi, parts, su_mag, _sv_mag, sv_store = channel_scale_inner(W_dev, suh, svh, dev)
-    else:
-        Wi, parts = _encode_inner(W_dev, suh, svh, dev)
-    Wscale_d = _rms_scale(parts, Wi.numel(), float(lut_rms), dev)
-    Wq = _div(Wi, Wscale_d)
-    del Wi
+    members = []
+    for W in Ws:
+        m_out = W.shape[0]
+        svh = sign_vec(m_out, su_seed + 1).half()
+        W_dev = W.detach().to(dev, non_blocking=True)
+        if W_dev.dtype not in DTYPE_IDS:
+            W_dev = W_dev.float()
+        W_dev = W_dev.contiguous()
+        mem = {"m_out": m_out, "svh": svh}
+        if channel_scales:
+            from .incoherence import channel_scale_inner
+            Wi, parts, mem["su_mag"], _sv_mag, mem["sv_store"] = channel_scale_inner(
+                W_dev, suh, svh, dev)
+        else:
+            Wi, parts = _encode_inner(W_dev, suh, svh, dev)
+        del W_dev
+        mem["Wscale_d"] = _rms_scale(parts, Wi.numel(), float(lut_rms), dev)
+        mem["Wq"] = _div(Wi, mem["Wscale_d"])
+        del Wi
+        members.append(mem)
 
     Lfac = None
     if use_ldlq and H_x is not None:
@@ -476,34 +516,49 @@ def quantize_linear(W: torch.Tensor, H_x: torch.Tensor | None, code: str = "exl3
         if progress is not None:
             progress("hinv", time.time() - t0)
 
-    pv = STEPS // 2 if pivot is None else int(pivot)
-    hatW, trl, st, _ = _sweep(Wq, Lfac, [K], [m_out], code, pv, margin, buf_cols,
-                              progress=progress, want_states=keep_states)
-    trellis = trl[0]
-    del Wq, Lfac
-    su32 = suh.float().to(dev)
-    sv32 = svh.float().to(dev)
-    if channel_scales:
-        from .incoherence import channel_scale_outer
-        W_hat, suh, svh = channel_scale_outer(hatW, suh, svh, su_mag, sv_store,
-                                              Wscale_d, dev)
+    widths = [m["m_out"] for m in members]
+    if len(members) == 1:
+        Wq = members[0].pop("Wq")
     else:
-        W_hat = torch.empty(m_out, k_in, dtype=torch.float32, device=dev)
-        call("exl3b_incoherence_inv", hatW.data_ptr(), k_in, m_out, Wscale_d.data_ptr(),
-             su32.data_ptr(), sv32.data_ptr(), W_hat.data_ptr(), _stream(dev))
+        Wq = torch.cat([m.pop("Wq") for m in members], dim=1)
+    pv = STEPS // 2 if pivot is None else int(pivot)
+    hatW, trl, st, _ = _sweep(Wq, Lfac, list(Ks), widths, code, pv, margin, buf_cols,
+                              progress=progress, want_states=keep_states)
+    del Wq, Lfac
+
     od = torch.device(out_device) if out_device is not None else dev
-    out = {
-        "W_hat": W_hat.to(od),
-        "trellis": trellis.to(od),
-        "suh": suh.to(od), "svh": svh.to(od),
-        "Wscale": float(Wscale_d.item()), "lut_rms": float(lut_rms),
-        "code": code, "K": K, "L": L, "V": 1, "use_ldlq": use_ldlq,
-        "channel_scales": channel_scales,
-    }
-    if keep_states:
-        out["states"] = st.to(od)
-        out["hatWq"] = hatW.to(od)
-    return out
+    outs = []
+    c0 = 0
+    for j, mem in enumerate(members):
+        m_out = mem["m_out"]
+        hw = hatW if len(members) == 1 else hatW[:, c0:c0 + m_out].contiguous()
+        su32 = suh.float().to(dev)
+        sv32 = mem["svh"].float().to(dev)
+        suh_j, svh_j = suh, mem["svh"]
+        if channel_scales:
+            from .incoherence import channel_scale_outer
+            W_hat, suh_j, svh_j = channel_scale_outer(hw, suh, mem["svh"], mem["su_mag"],
+                                                      mem["sv_store"], mem["Wscale_d"], dev)
+        else:
+            W_hat = torch.empty(m_out, k_in, dtype=torch.float32, device=dev)
+            call("exl3b_incoherence_inv", hw.data_ptr(), k_in, m_out,
+                 mem["Wscale_d"].data_ptr(), su32.data_ptr(), sv32.data_ptr(),
+                 W_hat.data_ptr(), _stream(dev))
+        out = {
+            "W_hat": W_hat.to(od),
+            "trellis": trl[j].to(od),
+            "suh": suh_j.to(od), "svh": svh_j.to(od),
+            "Wscale": float(mem["Wscale_d"].item()), "lut_rms": float(lut_rms),
+            "code": code, "K": int(Ks[j]), "L": L, "V": 1, "use_ldlq": use_ldlq,
+            "channel_scales": channel_scales,
+        }
+        if keep_states:
+            out["states"] = (st if len(members) == 1 else
+                             st[:, c0 // 16:(c0 + m_out) // 16].contiguous()).to(od)
+            out["hatWq"] = hw.to(od)
+        outs.append(out)
+        c0 += m_out
+    return outs
 
 
 def hessian_weighted_err(W: torch.Tensor, W_hat: torch.Tensor, H_x: torch.Tensor) -> float:

@@ -62,12 +62,14 @@ def config2(seed_w: int = 1, seed_h: int = 2, device="cuda"):
     return weight(HIDDEN, HIDDEN, 0.02, seed_w, device), hessian(HIDDEN, seed_h, device)
 
 
-def config3(device="cuda"):
+def config3(device="cuda", seed_offset: int = 0):
     """Config 3: fused qkv q 5120->6144, k/v 5120->1024 (seeds 3, 4, 5), one
-    shared Hessian (seed 6), K = [5, 7, 7]."""
-    Ws = [weight(6144, HIDDEN, 0.02, 3, device), weight(1024, HIDDEN, 0.02, 4, device),
-          weight(1024, HIDDEN, 0.02, 5, device)]
-    return Ws, hessian(HIDDEN, 6, device), [5, 7, 7]
+    shared Hessian (seed 6), K = [5, 7, 7].  seed_offset shifts every seed
+    (independent problems per rank)."""
+    o = int(seed_offset)
+    Ws = [weight(6144, HIDDEN, 0.02, 3 + o, device), weight(1024, HIDDEN, 0.02, 4 + o, device),
+          weight(1024, HIDDEN, 0.02, 5 + o, device)]
+    return Ws, hessian(HIDDEN, 6 + o, device), [5, 7, 7]
 
 
 def config4(device="cuda", seed_w: int = 7, seed_h: int = 8):
@@ -78,3 +80,25 @@ def config4(device="cuda", seed_w: int = 7, seed_h: int = 8):
 
 def stack_seed(layer: int, tensor: str) -> int:
     return 1000 * (layer + 1) + [n for n, _, _ in STACK_SHAPES].index(tensor)
+
+
+# Input groups of one layer: the tensors that read the same activations share
+# one Hessian (name, input dim, member tensors in fused-module order).
+STACK_GROUPS = [("attn", HIDDEN, ["q", "k", "v"]), ("o", 6144, ["o"]),
+                ("mlp", HIDDEN, ["gate", "up"]), ("down", INTER, ["down"])]
+
+
+def stack_hessian_seed(layer: int, group: str) -> int:
+    return 1000 * (layer + 1) + 100 + [g for g, _, _ in STACK_GROUPS].index(group)
+
+
+def stack_weight(layer: int, tensor: str, device) -> torch.Tensor:
+    """Weight `tensor` of layer `layer` of the 27B-shape stack (sigma 0.02,
+    0.015 for the down projection, like configs 2 and 4)."""
+    out_f, in_f = {n: (o, i) for n, o, i in STACK_SHAPES}[tensor]
+    std = 0.015 if tensor == "down" else 0.02
+    return weight(out_f, in_f, std, stack_seed(layer, tensor), device)
+
+
+def stack_weights_per_layer() -> int:
+    return sum(o * i for _, o, i in STACK_SHAPES)

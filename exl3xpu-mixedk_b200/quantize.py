@@ -14,6 +14,7 @@ from exl3b.api import (  # noqa: F401
     prepare_incoherence,
     quantize,
     quantize_linear,
+    quantize_linear_fused,
     quantize_seq_tailbite,
     rel_mse,
     rotate_hessian,

@@ -61,9 +61,11 @@ long long exl3b_launch_count(void);
 /* Per-launch CUDA-event timing of the dominant kernels, on the stream each
  * is launched on.  exl3b_profile_begin() starts recording; exl3b_profile_end
  * stops, synchronises the recorded events and returns, for `kind`
- * (0 = fused LDLQ tile kernel, 1 = feedback GEMM, 2 = standalone encoder),
+ * (0 = fused LDLQ tile kernel, 1 = feedback GEMM, 2 = standalone encoder,
+ * 3 = Hadamard rotations of W / W_hat / H, 4 = block LDL factorisation),
  * the summed duration, the launch count and the summed work units
- * (0, 2: weights encoded; 1: FLOP). */
+ * (0, 2: weights encoded; 1: useful FLOP; 3: algorithmic bytes; 4: k^3/3
+ * FLOP). */
 void exl3b_profile_begin(void);
 int exl3b_profile_end(int kind, double* ms_total, long long* launches, double* units);
 

@@ -273,3 +273,43 @@ def test_feedback_gemm_tcgen05(M, N, K):
     err = (C.double() - ref).abs().max().item()
     scale = (A[:, :M].double().abs().t() @ B[:, :N].double().abs()).max().item()
     assert err <= 2e-6 * scale, (err, scale)
+
+
+@pytest.mark.parametrize("channel_scales", (False, True))
+def test_quantize_linear_fused_equals_members(xq, channel_scales):
+    """A mixed-K fused module (q/k/v-like members sharing H, K = [5, 7, 7]):
+    one shared LDL + one sweep over the members side by side is bit-identical
+    to quantize_linear member by member."""
+    k = 256
+    sizes, Ks = [256, 128, 128], [5, 7, 7]
+    gen = torch.Generator().manual_seed(44)
+    A = torch.randn(k, k, generator=gen)
+    H = A.t() @ A / k + 0.1 * torch.eye(k)
+    Ws = [torch.randn(m, k, generator=gen) * 0.02 for m in sizes]
+    fused = xq.quantize_linear_fused(Ws, H, Ks=Ks, channel_scales=channel_scales,
+                                     device="cuda")
+    for W, K, r in zip(Ws, Ks, fused):
+        s = xq.quantize_linear(W, H, K=K, channel_scales=channel_scales, device="cuda")
+        assert r["K"] == K and r["trellis"].shape == (k // 16, W.shape[0] // 16, 16 * K)
+        assert torch.equal(r["trellis"], s["trellis"])
+        assert torch.equal(r["W_hat"], s["W_hat"])
+        assert torch.equal(r["suh"], s["suh"]) and torch.equal(r["svh"], s["svh"])
+        assert r["Wscale"] == s["Wscale"]
+
+
+def test_stored_fields_dequantise_to_w_hat(xq, tmp_path):
+    """Written EXL3 fields reproduce W_hat: bit-exact on the channel-scales
+    path (suh/svh already fp16 and folded), within the fp16 rounding of the
+    folded Wscale on the plain path."""
+    from exl3b import export as ex
+    W, H = _ldlq_problem(256, 128, 45)
+    for cs in (True, False):
+        r = xq.quantize_linear(W, H, K=4, channel_scales=cs, device="cuda")
+        path = ex.save_quantized(tmp_path, 3, "self_attn.o_proj", r)
+        f = ex.load_quantized(path)
+        w = ex.weight_orig(f["trellis"], f["suh"], f["svh"], f["meta"]["K"]).t().cpu()
+        if cs:
+            assert torch.equal(w, r["W_hat"])
+        else:
+            rel = (w - r["W_hat"]).abs().max() / r["W_hat"].abs().max()
+            assert rel <= 1e-3, rel

@@ -106,3 +106,30 @@ def test_workspace_validation(ops):
     rc = L.exl3b_tailbite(X.data_ptr(), 4, 4, 0, 0, 0, S.data_ptr(), None, 0, None)
     assert rc == 0, native.last_error()
     torch.cuda.synchronize()
+
+
+def test_serve_worker_matches_oracle(oracle, mul1_lut):
+    """The exl3b_vit worker over the framed protocol (the reference's "proc"
+    transport) returns the oracle's states, chunked across frames."""
+    import torch
+    from exl3b import transport as tp
+    rng = np.random.default_rng(77)
+    X = rng.standard_normal((37, 256)).astype(np.float32)
+    ref = oracle.tailbite(X, mul1_lut, 4, pivot=128, margin=0, nthreads=NTHREADS)
+    w = tp.ServeWorker(devidx=0)
+    try:
+        assert np.array_equal(w.run(X, "mul1p", 0, 128), ref)
+        ref2 = oracle.tailbite(X, mul1_lut, 4, pivot=0, margin=16, nthreads=NTHREADS)
+        assert np.array_equal(w.run(X, "mul1", 16, 0), ref2)
+        # rc passthrough: bad pivot is xtq_vit_run's rc 7, worker keeps serving
+        rc, _ = w.request(1, 0, 300, 2, 2048, "mul1p", X[:2])
+        assert rc == 7
+        assert np.array_equal(w.run(X[:5], "mul1p", 0, 128), ref[:5])
+    finally:
+        assert w.close() == 0
+    os.environ["XTQ_VIT_MAXSEQ"] = "16"
+    try:
+        st = tp.tailbite_proc(torch.from_numpy(X).t(), pivot=128, margin=0)
+    finally:
+        del os.environ["XTQ_VIT_MAXSEQ"]
+    assert np.array_equal(st.t().numpy(), ref.astype(np.int64))
