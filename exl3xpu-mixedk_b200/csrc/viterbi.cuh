@@ -20,7 +20,8 @@
 //    512 threads owns 128 fixed states (whole butterflies for K <= 3, a slice of
 //    one butterfly for K >= 4) and holds their decode values in 64 packed-fp16
 //    registers for the whole kernel (EXL3 decode values are exact in fp16), so
-//    one add-compare-select is: mixed fp16-fp32 sub, fmul, fadd, compare, 2 selects --
+//    one add-compare-select is: mixed fp16-fp32 sub, fmul, fadd, compare, 2
+//    predicated FMA-pipe updates --
 //    no shared-memory gather on the inner loop.
 //  * Backpointers: each thread packs its outputs' K-bit argmins into one
 //    8/16/32/64-bit word per step and stores it coalesced to global scratch
@@ -143,66 +144,77 @@ __device__ __forceinline__ void vit_load_f2tab(__half2 (&f2)[64],
     }
 }
 
-// d = fl(f - x) with f the low (HI=false) or high half of a packed pair.  The
-// sm_100 mixed-precision subtract takes the fp16 half directly (exact widening,
-// one fp32 rounding), so this is one instruction and bit-identical to
-// fl(float(f) - x).  Keeping it in an asm block that consumes x also stops the
-// compiler from hoisting 128 unpacked decode values out of the step loop
-// (which would need 128 extra registers).
-template <bool HI>
-__device__ __forceinline__ float sub_f16(__half2 h2, float x) {
+// Compare-and-update of one add-compare-select: if c < best then best = c and
+// idx = W.  Strict < keeps the first (lowest) predecessor on ties, like
+// torch.min.  Only the compare runs on the (half-rate) ALU pipe: both updates
+// are predicated FMA-pipe instructions -- best = c + 0 (exact: costs are >= +0
+// or +inf) and idx = 0 * 0 + W (the index held as a small float).  `zr` is a
+// zero the compiler cannot see through (it comes from a volatile shared-memory
+// load), so neither update folds back into an ALU move.
+template <int W>
+__device__ __forceinline__ void acs_update(float& best, float& idx, float c, float zr) {
+    asm("{\n\t.reg .pred p;\n\t"
+        "setp.lt.f32 p, %2, %0;\n\t"
+        "@p add.rn.f32 %0, %2, %3;\n\t"
+        "@p fma.rn.f32 %1, %3, %3, %4;\n\t}"
+        : "+f"(best), "+f"(idx)
+        : "f"(c), "f"(zr), "f"((float)W));
+}
+
+// Costs of predecessors W and W + 1 of one output -- the low and high halves
+// of one packed decode register: c = fl(fl(f - x)^2) + bw for both.  The
+// sm_100 mixed-precision subtract takes each fp16 half directly (exact
+// widening, one fp32 rounding: bit-identical to fl(float(f) - x)); the square
+// and the add are one packed fp32x2 multiply and one packed add (IEEE
+// round-to-nearest in each lane, identical to the scalar operations).  bw2
+// holds (best_i of predecessor W, of W + 1).  The unpack sits in the same asm
+// block as the subtractions, which consume x, so the compiler cannot hoist 128
+// unpacked decode values out of the step loop (128 extra registers).
+__device__ __forceinline__ void cost_pair(__half2 h2, float x, uint64_t bw2, float& c0,
+                                          float& c1) {
     const uint32_t r = *reinterpret_cast<const uint32_t*>(&h2);
+    asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 d0, d1;\n\t.reg .b64 dd, cc;\n\t"
+        "mov.b32 {lo, hi}, %2;\n\t"
+        "sub.rn.f32.f16 d0, lo, %3;\n\t"
+        "sub.rn.f32.f16 d1, hi, %3;\n\t"
+        "mov.b64 dd, {d0, d1};\n\t"
+        "mul.rn.f32x2 dd, dd, dd;\n\t"
+        "add.rn.f32x2 cc, dd, %4;\n\t"
+        "mov.b64 {%0, %1}, cc;\n\t}"
+        : "=f"(c0), "=f"(c1) : "r"(r), "f"(x), "l"(bw2));
+}
+
+__device__ __forceinline__ float min3(float a, float b, float c) {
     float d;
-    if (HI)
-        asm("{\n\t.reg .b16 lo, hi;\n\t"
-            "mov.b32 {lo, hi}, %1;\n\t"
-            "sub.rn.f32.f16 %0, hi, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
-    else
-        asm("{\n\t.reg .b16 lo, hi;\n\t"
-            "mov.b32 {lo, hi}, %1;\n\t"
-            "sub.rn.f32.f16 %0, lo, %2;\n\t}" : "=f"(d) : "r"(r), "f"(x));
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
 
-template <int K>
-__device__ __forceinline__ float vit_d(const __half2 (&f2)[64], int r, float x) {
-    return (r & 1) ? sub_f16<true>(f2[r >> 1], x) : sub_f16<false>(f2[r >> 1], x);
-}
-
-// Compare-and-update of one add-compare-select: if c < best then best = c and
-// idx = W.  Strict < keeps the first (lowest) predecessor on ties, like
-// torch.min.  W is an immediate, so this issues as setp + two predicated moves.
-template <int W>
-__device__ __forceinline__ void acs_update(float& best, int& idx, float c) {
-    asm("{\n\t.reg .pred p;\n\t"
-        "setp.lt.f32 p, %2, %0;\n\t"
-        "@p mov.f32 %0, %2;\n\t"
-        "@p mov.b32 %1, %3;\n\t}"
-        : "+f"(best), "+r"(idx)
-        : "f"(c), "n"(W));
-}
-
 // TRACK = false: the step's backpointers are never read (pass-1 steps before
-// the traceback stop), so only the minimum is kept: one min instead of a
-// compare and two selects.  The minimum value is the same either way.
+// the traceback stop), so only the minimum is kept: one three-input min per
+// predecessor pair instead of compares and selects.  The minimum value is the
+// same either way.
 template <int K, int W, int NJ, int NCH, bool TRACK>
-struct AcsRow {
-    // one predecessor w = W for all NJ outputs of butterfly slice b
-    static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x, float bw,
+struct AcsPair {
+    // predecessors W, W + 1 (W even) for all NJ outputs of butterfly slice b
+    static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x, uint64_t bw2,
                                                int b, float (&best)[NJ][NCH],
-                                               int (&bi)[NJ][NCH]) {
-        constexpr int ch = W % NCH;
+                                               float (&bi)[NJ][NCH], float zr) {
+        constexpr int ch0 = W % NCH, ch1 = (W + 1) % NCH;
 #pragma unroll
         for (int u = 0; u < NJ; ++u) {
-            const float d = vit_d<K>(f2, (b * NJ + u) * (1 << K) + W, x);
-            const float c = __fadd_rn(__fmul_rn(d, d), bw);
-            if (W < NCH) {
-                best[u][ch] = c;
-                if (TRACK) bi[u][ch] = W;
-            } else if (TRACK) {
-                acs_update<W>(best[u][ch], bi[u][ch], c);
+            float c0, c1;
+            cost_pair(f2[(((b * NJ + u) << K) + W) >> 1], x, bw2, c0, c1);
+            if (TRACK) {
+                if (W < NCH) { best[u][ch0] = c0; bi[u][ch0] = (float)W; }
+                else acs_update<W>(best[u][ch0], bi[u][ch0], c0, zr);
+                if (W + 1 < NCH) { best[u][ch1] = c1; bi[u][ch1] = (float)(W + 1); }
+                else acs_update<W + 1>(best[u][ch1], bi[u][ch1], c1, zr);
+            } else if (NCH == 1) {
+                best[u][0] = (W == 0) ? fminf(c0, c1) : min3(best[u][0], c0, c1);
             } else {
-                best[u][ch] = fminf(best[u][ch], c);
+                best[u][ch0] = (W < NCH) ? c0 : fminf(best[u][ch0], c0);
+                best[u][ch1] = (W + 1 < NCH) ? c1 : fminf(best[u][ch1], c1);
             }
         }
     }
@@ -212,16 +224,20 @@ template <int K, int W, int NJ, int NCH, bool TRACK>
 struct AcsLoop {
     static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x,
                                                const float (&bin)[1 << K], int b,
-                                               float (&best)[NJ][NCH], int (&bi)[NJ][NCH]) {
-        AcsRow<K, W, NJ, NCH, TRACK>::run(f2, x, bin[W], b, best, bi);
-        AcsLoop<K, W + 1, NJ, NCH, TRACK>::run(f2, x, bin, b, best, bi);
+                                               float (&best)[NJ][NCH], float (&bi)[NJ][NCH],
+                                               float zr) {
+        uint64_t bw2;
+        asm("mov.b64 %0, {%1, %2};" : "=l"(bw2) : "f"(bin[W]), "f"(bin[W + 1]));
+        AcsPair<K, W, NJ, NCH, TRACK>::run(f2, x, bw2, b, best, bi, zr);
+        AcsLoop<K, W + 2, NJ, NCH, TRACK>::run(f2, x, bin, b, best, bi, zr);
     }
 };
 template <int K, int NJ, int NCH, bool TRACK>
 struct AcsLoop<K, (1 << K), NJ, NCH, TRACK> {
     static __device__ __forceinline__ void run(const __half2 (&)[64], float,
                                                const float (&)[1 << K], int,
-                                               float (&)[NJ][NCH], int (&)[NJ][NCH]) {}
+                                               float (&)[NJ][NCH], float (&)[NJ][NCH],
+                                               float) {}
 };
 
 // Butterfly inputs best_i[m + w*P], w < 2^K, into registers.
@@ -247,7 +263,7 @@ __device__ __forceinline__ void vit_load_bin(const float* __restrict__ Bc, int m
 template <int K, bool TRACK = true>
 __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
                                              const float* __restrict__ Bc,
-                                             float* __restrict__ Bn, int t) {
+                                             float* __restrict__ Bn, int t, float zr) {
     using G = Geo<K>;
     constexpr int NCH = G::NCH;
     constexpr int NJ = G::NJ;
@@ -256,16 +272,16 @@ __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
     for (int b = 0; b < G::NB; ++b) {
         const int m = G::bfly(t, b);
         float best[NJ][NCH];
-        int bi[NJ][NCH];
+        float bi[NJ][NCH];
         float bin[1 << K];
         vit_load_bin<K>(Bc, m, bin);
-        AcsLoop<K, 0, NJ, NCH, TRACK>::run(f2, x, bin, b, best, bi);
+        AcsLoop<K, 0, NJ, NCH, TRACK>::run(f2, x, bin, b, best, bi, zr);
 #pragma unroll
         for (int u = 0; u < NJ; ++u) {
             float bv = best[u][0];
             const int e = b * NJ + u;
             if (TRACK) {
-                int bx = bi[u][0];
+                float bx = bi[u][0];
 #pragma unroll
                 for (int ch = 1; ch < NCH; ++ch) {   // (value, index) lexicographic
                     const bool take =
@@ -273,7 +289,7 @@ __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
                     bv = take ? best[u][ch] : bv;
                     bx = take ? bi[u][ch] : bx;
                 }
-                bits |= static_cast<uint64_t>(bx) << (e * G::BPE);
+                bits |= static_cast<uint64_t>(__float2uint_rz(bx)) << (e * G::BPE);
             } else {
 #pragma unroll
                 for (int ch = 1; ch < NCH; ++ch) bv = fminf(bv, best[u][ch]);
@@ -318,25 +334,30 @@ __device__ __forceinline__ int vit_pass(const __half2 (&f2)[64], char* smem, int
     float* redc = reinterpret_cast<float*>(smem + SM::OFF_RED);
     int* reds = reinterpret_cast<int*>(smem + SM::OFF_RED + 64);
     int* bcast = reinterpret_cast<int*>(smem + SM::OFF_RED + 128);
+    float* zword = reinterpret_cast<float*>(smem + SM::OFF_RED + 192);
     const float INF = __int_as_float(0x7f800000);
+    if (t == 0) *zword = 0.0f;
 
     // best_0: 0 (free) or 0 at `overlap`, +inf elsewhere -> cost_0 = E_0 + mask
     for (int idx = t; idx < G::SPRE; idx += kVT)
         Bc[G::baddr(idx)] = (overlap < 0 || idx == overlap) ? 0.0f : INF;
     __syncthreads();
+    float zr;
+    asm volatile("ld.volatile.shared.f32 %0, [%1];" : "=f"(zr)
+                 : "r"((uint32_t)__cvta_generic_to_shared(zword)));
 
     // steps whose backpointer row lies at or before `stop` are never traced
     // back through: minimum only
     const int nfree = min(max(stop, 0), nsteps - 1);
     for (int i = 0; i < nfree; ++i) {
         const float x = xs[(i - rol) & 255];
-        vit_step<K, false>(f2, x, Bc, Bn, t);
+        vit_step<K, false>(f2, x, Bc, Bn, t, zr);
         float* tmp = Bc; Bc = Bn; Bn = tmp;
         __syncthreads();
     }
     for (int i = nfree; i < nsteps - 1; ++i) {
         const float x = xs[(i - rol) & 255];
-        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t);
+        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t, zr);
         vit_store_bits<K>(bp + (size_t)(i + 1) * G::BP_ROW, bits, t);
         float* tmp = Bc; Bc = Bn; Bn = tmp;
         __syncthreads();
@@ -350,7 +371,7 @@ __device__ __forceinline__ int vit_pass(const __half2 (&f2)[64], char* smem, int
     // elsewhere) keeps only group j == overlap.
     {
         const float x = xs[(nsteps - 1 - rol) & 255];
-        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t);
+        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t, zr);
         float bc = INF;
         int bs = 0x7fffffff;
 #pragma unroll
