@@ -53,11 +53,14 @@ struct Geo {
     static constexpr int BPTB = NOUT * BPE / 8;       // backpointer bytes / thread / step
     static constexpr int BP_ROW = kVT * BPTB;         // backpointer bytes per step
     static constexpr int TB_ROWS = kTbBytes / BP_ROW; // rows per traceback chunk
-    // best-array smem layout: transposed for K >= 5 (16-byte loads of a
-    // butterfly's inputs); natural for K <= 4, where a transposed layout turns
-    // every output store into a bank conflict (a warp's lanes write rows 8
-    // apart in one column)
-    static constexpr bool TRANSPOSED = K >= 5;
+    // best-array smem layout: transposed for K >= 6 (a butterfly's 64 or 128
+    // inputs as 16-byte loads); natural for K <= 5, where a butterfly's 2^K
+    // inputs are loads that a warp's lanes share or spread over distinct
+    // banks -- a transposed layout there turns every output store into an 8-
+    // to 16-way bank conflict (a warp's lanes write rows apart in one column).
+    // (16-byte output stores measured slower than scalar ones: the extra live
+    // registers cost more than the conflicts they remove.)
+    static constexpr bool TRANSPOSED = K >= 6;
     // transposed row stride: NC floats, padded by 4 when a row is < 32 words
     // so that four consecutive butterflies start in different bank groups
     static constexpr int ROW = (NC < 32) ? NC + 4 : NC;
@@ -148,9 +151,11 @@ __device__ __forceinline__ void vit_load_f2tab(__half2 (&f2)[64],
 // idx = W.  Strict < keeps the first (lowest) predecessor on ties, like
 // torch.min.  Only the compare runs on the (half-rate) ALU pipe: both updates
 // are predicated FMA-pipe instructions -- best = c + 0 (exact: costs are >= +0
-// or +inf) and idx = 0 * 0 + W (the index held as a small float).  `zr` is a
-// zero the compiler cannot see through (it comes from a volatile shared-memory
-// load), so neither update folds back into an ALU move.
+// or +inf) and idx = 0 * 0 + W, the index held as the float whose bit pattern
+// is W (a subnormal; fp32 arithmetic without flush-to-zero keeps it exact), so
+// reading it back is a bit cast.  `zr` is a zero the compiler cannot see
+// through (it comes from a volatile shared-memory load), so neither update
+// folds back into an ALU move.
 template <int W>
 __device__ __forceinline__ void acs_update(float& best, float& idx, float c, float zr) {
     asm("{\n\t.reg .pred p;\n\t"
@@ -158,7 +163,7 @@ __device__ __forceinline__ void acs_update(float& best, float& idx, float c, flo
         "@p add.rn.f32 %0, %2, %3;\n\t"
         "@p fma.rn.f32 %1, %3, %3, %4;\n\t}"
         : "+f"(best), "+f"(idx)
-        : "f"(c), "f"(zr), "f"((float)W));
+        : "f"(c), "f"(zr), "f"(__uint_as_float((uint32_t)W)));
 }
 
 // Costs of predecessors W and W + 1 of one output -- the low and high halves
@@ -206,9 +211,9 @@ struct AcsPair {
             float c0, c1;
             cost_pair(f2[(((b * NJ + u) << K) + W) >> 1], x, bw2, c0, c1);
             if (TRACK) {
-                if (W < NCH) { best[u][ch0] = c0; bi[u][ch0] = (float)W; }
+                if (W < NCH) { best[u][ch0] = c0; bi[u][ch0] = __uint_as_float((uint32_t)W); }
                 else acs_update<W>(best[u][ch0], bi[u][ch0], c0, zr);
-                if (W + 1 < NCH) { best[u][ch1] = c1; bi[u][ch1] = (float)(W + 1); }
+                if (W + 1 < NCH) { best[u][ch1] = c1; bi[u][ch1] = __uint_as_float((uint32_t)(W + 1)); }
                 else acs_update<W + 1>(best[u][ch1], bi[u][ch1], c1, zr);
             } else if (NCH == 1) {
                 best[u][0] = (W == 0) ? fminf(c0, c1) : min3(best[u][0], c0, c1);
@@ -276,6 +281,7 @@ __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
         float bin[1 << K];
         vit_load_bin<K>(Bc, m, bin);
         AcsLoop<K, 0, NJ, NCH, TRACK>::run(f2, x, bin, b, best, bi, zr);
+        float outv[NJ];
 #pragma unroll
         for (int u = 0; u < NJ; ++u) {
             float bv = best[u][0];
@@ -289,13 +295,15 @@ __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
                     bv = take ? best[u][ch] : bv;
                     bx = take ? bi[u][ch] : bx;
                 }
-                bits |= static_cast<uint64_t>(__float2uint_rz(bx)) << (e * G::BPE);
+                bits |= static_cast<uint64_t>(__float_as_uint(bx)) << (e * G::BPE);
             } else {
 #pragma unroll
                 for (int ch = 1; ch < NCH; ++ch) bv = fminf(bv, best[u][ch]);
             }
-            Bn[G::baddr(G::out_j(t, e))] = bv;
+            outv[u] = bv;
         }
+#pragma unroll
+        for (int u = 0; u < NJ; ++u) Bn[G::baddr(G::out_j(t, b * NJ + u))] = outv[u];
     }
     return bits;
 }
