@@ -65,6 +65,9 @@ struct Geo {
     // so that four consecutive butterflies start in different bank groups
     static constexpr int ROW = (NC < 32) ? NC + 4 : NC;
     static constexpr int NCH = (NJ >= 4) ? 1 : 4 / NJ;  // partial min chains
+    // traced steps update (best, idx) once per predecessor pair instead of
+    // once per candidate (measured faster at these K, slower at K = 3..5)
+    static constexpr bool PAIR_UPDATE = (K == 2) || (K >= 6);
 
     // output index j of thread t's e-th output
     static __device__ __forceinline__ int out_j(int t, int e) {
@@ -175,6 +178,8 @@ __device__ __forceinline__ void acs_update(float& best, float& idx, float c, flo
 // holds (best_i of predecessor W, of W + 1).  The unpack sits in the same asm
 // block as the subtractions, which consume x, so the compiler cannot hoist 128
 // unpacked decode values out of the step loop (128 extra registers).
+// (Computing one of the two differences as a mixed-precision FMA, f * 1 - x,
+// moves it to the FMA pipe but measured slower.)
 __device__ __forceinline__ void cost_pair(__half2 h2, float x, uint64_t bw2, float& c0,
                                           float& c1) {
     const uint32_t r = *reinterpret_cast<const uint32_t*>(&h2);
@@ -195,31 +200,62 @@ __device__ __forceinline__ float min3(float a, float b, float c) {
     return d;
 }
 
+// Both candidates of a predecessor pair against (best, idx), equivalent to the
+// two strict-< updates in ascending order (first index on ties):
+//   m = min(best, c0, c1); improved = m < best;
+//   the winner is W + 1 exactly when improved and c0 != m (c0 == m means W
+//   wins, also when c1 == c0).
+// Three ALU instructions (min, two compares) and two predicated FMA-pipe index
+// writes (the subnormal-bit-pattern index of acs_update); best = m is a rename.
+template <int W>
+__device__ __forceinline__ void acs_update_pair(float& best, float& idx, float c0, float c1,
+                                                float zr) {
+    asm("{\n\t.reg .pred p, q;\n\t.reg .f32 m;\n\t"
+        "min.f32 m, %0, %2, %3;\n\t"
+        "setp.lt.f32 p, m, %0;\n\t"
+        "setp.ne.and.f32 q, %2, m, p;\n\t"
+        "@p fma.rn.f32 %1, %4, %4, %5;\n\t"
+        "@q fma.rn.f32 %1, %4, %4, %6;\n\t"
+        "mov.f32 %0, m;\n\t}"
+        : "+f"(best), "+f"(idx)
+        : "f"(c0), "f"(c1), "f"(zr), "f"(__uint_as_float((uint32_t)W)),
+          "f"(__uint_as_float((uint32_t)(W + 1))));
+}
+
 // TRACK = false: the step's backpointers are never read (pass-1 steps before
 // the traceback stop), so only the minimum is kept: one three-input min per
 // predecessor pair instead of compares and selects.  The minimum value is the
 // same either way.
+// TRACK = true: per-candidate compare-and-update (acs_update) or, where it
+// measured faster (Geo::PAIR_UPDATE: K = 2 and K >= 6), one update per pair
+// (acs_update_pair).  Partial chains (NCH > 1, for the small-NJ shapes K >= 6)
+// take whole pairs: chain (W / 2) mod NCH; each chain sees its candidates in
+// ascending order, and the chains merge lexicographically on (value, index).
 template <int K, int W, int NJ, int NCH, bool TRACK>
 struct AcsPair {
     // predecessors W, W + 1 (W even) for all NJ outputs of butterfly slice b
     static __device__ __forceinline__ void run(const __half2 (&f2)[64], float x, uint64_t bw2,
                                                int b, float (&best)[NJ][NCH],
                                                float (&bi)[NJ][NCH], float zr) {
-        constexpr int ch0 = W % NCH, ch1 = (W + 1) % NCH;
+        constexpr int ch = (W >> 1) % NCH;
+        constexpr bool first = (W >> 1) < NCH;
 #pragma unroll
         for (int u = 0; u < NJ; ++u) {
             float c0, c1;
             cost_pair(f2[(((b * NJ + u) << K) + W) >> 1], x, bw2, c0, c1);
             if (TRACK) {
-                if (W < NCH) { best[u][ch0] = c0; bi[u][ch0] = __uint_as_float((uint32_t)W); }
-                else acs_update<W>(best[u][ch0], bi[u][ch0], c0, zr);
-                if (W + 1 < NCH) { best[u][ch1] = c1; bi[u][ch1] = __uint_as_float((uint32_t)(W + 1)); }
-                else acs_update<W + 1>(best[u][ch1], bi[u][ch1], c1, zr);
-            } else if (NCH == 1) {
-                best[u][0] = (W == 0) ? fminf(c0, c1) : min3(best[u][0], c0, c1);
+                if (first) {
+                    best[u][ch] = c0;
+                    bi[u][ch] = __uint_as_float((uint32_t)W);
+                    acs_update<W + 1>(best[u][ch], bi[u][ch], c1, zr);
+                } else if (Geo<K>::PAIR_UPDATE) {
+                    acs_update_pair<W>(best[u][ch], bi[u][ch], c0, c1, zr);
+                } else {
+                    acs_update<W>(best[u][ch], bi[u][ch], c0, zr);
+                    acs_update<W + 1>(best[u][ch], bi[u][ch], c1, zr);
+                }
             } else {
-                best[u][ch0] = (W < NCH) ? c0 : fminf(best[u][ch0], c0);
-                best[u][ch1] = (W + 1 < NCH) ? c1 : fminf(best[u][ch1], c1);
+                best[u][ch] = first ? fminf(c0, c1) : min3(best[u][ch], c0, c1);
             }
         }
     }
