@@ -179,12 +179,6 @@ static int grow(uint8_t** p, size_t* have, size_t want) {
     return RC_OK;
 }
 
-static int tailbite_grid(int nseq) {
-    const int sms = device_sms();
-    if (sms <= 0) return 0;
-    return nseq < sms ? nseq : sms;
-}
-
 }  // namespace exl3b
 
 using namespace exl3b;
@@ -244,7 +238,7 @@ int exl3b_device_init(int device) {
 
 size_t exl3b_tailbite_workspace_bytes(int nseq, int K) {
     if (K < 2 || K > 7 || nseq <= 0) return 0;
-    return (size_t)tailbite_grid(nseq) * bp_slot_bytes(K);
+    return tailbite_plan(nseq, K, device_sms()).bytes;
 }
 
 int exl3b_tailbite(const float* dX, int nseq, int K, int code, int pivot,
@@ -264,8 +258,8 @@ int exl3b_tailbite(const float* dX, int nseq, int K, int code, int pivot,
     DeviceState* st = nullptr;
     int rc = device_state(&st);
     if (rc) return rc;
-    const int grid = tailbite_grid(nseq);
-    const size_t need = (size_t)grid * bp_slot_bytes(K);
+    const TailbitePlan plan = tailbite_plan(nseq, K, st->sms);
+    const size_t need = plan.bytes;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     if (ws) {
         if (workspace_bytes < need || ((uintptr_t)ws & 255)) {
@@ -282,8 +276,8 @@ int exl3b_tailbite(const float* dX, int nseq, int K, int code, int pivot,
     const uint4* tab = nullptr;
     rc = f2tab_get(st, code, K, &tab);
     if (rc) return rc;
-    return launch_tailbite(dX, nseq, K, pivot, margin, dStates, ws, grid, tab,
-                           static_cast<cudaStream_t>(stream));
+    return launch_tailbite(dX, nseq, K, pivot, margin, dStates, ws, plan, tab,
+                           st->lut32[code], static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------------------------
@@ -339,8 +333,8 @@ int xtq_vit_run(const float* X, int nseq, const char* code, int margin,
         return RC_BAD_NSEQ;
     }
     const int K = 4;
-    const int grid = tailbite_grid(nseq);
-    const size_t dev_bytes = (size_t)nseq * kSteps * 8 + (size_t)grid * bp_slot_bytes(K);
+    const TailbitePlan plan = tailbite_plan(nseq, K, st->sms);
+    const size_t dev_bytes = (size_t)nseq * kSteps * 8 + plan.bytes;
     if ((long long)dev_bytes > env_ll("XTQ_VIT_MAXBYTES", 6LL << 30)) {
         fprintf(stderr, "xtq_vit: nseq %d over XTQ_VIT_MAXBYTES\n", nseq);
         set_error("nseq %d over XTQ_VIT_MAXBYTES", nseq);
@@ -367,13 +361,13 @@ int xtq_vit_run(const float* X, int nseq, const char* code, int margin,
         }
         st->stage_seqs = (size_t)nseq;
     }
-    rc = grow(&st->scratch, &st->scratch_bytes, (size_t)grid * bp_slot_bytes(K));
+    rc = grow(&st->scratch, &st->scratch_bytes, plan.bytes);
     if (rc) return rc;
     if (check_cuda(cudaMemcpy(st->stageX, X, (size_t)nseq * kSteps * 4,
                               cudaMemcpyHostToDevice), "xtq_vit_run H2D"))
         return RC_DEVICE_ERROR;
     rc = launch_tailbite(st->stageX, nseq, K, pivot, margin, st->stageS,
-                         st->scratch, grid, tab, 0);
+                         st->scratch, plan, tab, st->lut32[CODE_MUL1], 0);
     if (rc) return rc;
     if (check_cuda(cudaMemcpy(out, st->stageS, (size_t)nseq * kSteps * 4,
                               cudaMemcpyDeviceToHost), "xtq_vit_run D2H"))

@@ -50,10 +50,16 @@ int f2tab_get(DeviceState* st, int code, int K, const uint4** out);
 int build_f2tab(int K, const __half* lut16, uint4* tab, cudaStream_t stream);
 
 // Tail-biting encode of nseq sequences X [nseq][256] -> states [nseq][256].
-// ws must hold grid * bp_slot_bytes(K) bytes.
+// Standalone encoder plan for (nseq, K) on a device with `sms` SMs: the
+// lazy-argmin pipeline (K >= 4, at least two sequences per SM; grid = SMs,
+// two row regions per CTA) or the traced encoder (grid = min(nseq, SMs),
+// one backpointer slot per CTA); bytes = workspace needed.
+struct TailbitePlan { bool lazy; int grid; size_t bytes; };
+TailbitePlan tailbite_plan(int nseq, int K, int sms);
+size_t lazy_region_bytes(int K);
 int launch_tailbite(const float* dX, int nseq, int K, int pivot, int margin,
-                    int32_t* dStates, uint8_t* ws, int grid,
-                    const uint4* f2tab, cudaStream_t stream);
+                    int32_t* dStates, uint8_t* ws, const TailbitePlan& plan,
+                    const uint4* f2tab, const float* lut32, cudaStream_t stream);
 
 // ------------------------------------------------------------ incoherence
 struct HadParams {

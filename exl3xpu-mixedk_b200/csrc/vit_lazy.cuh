@@ -1,0 +1,251 @@
+// vit_lazy.cuh -- tail-biting Viterbi with the argmin taken lazily (K >= 4).
+//
+// Same trellis, costs and results as vit_tailbite (viterbi.cuh), bit for bit:
+// only where each step's predecessor choice is decided changes.
+//
+//  * Forward passes keep the minimum only (the "untraced" ACS: two
+//    subtractions, one packed square, one packed add, one three-input min per
+//    predecessor pair -- about half the work of tracking the argmin), and each
+//    thread streams its outputs best_{i+1}[j] of every step the traceback will
+//    cross to a per-tile row region in global memory (natural index order,
+//    row q = best_q).  Only the last step of a pass tracks its argmin (the
+//    final first-index argmin of the pass).
+//  * The traceback recomputes, for the one group j = s >> K on the path, the
+//    2^K candidate costs cost_{r-1}(j + w 2^(16-K)) = fl(fl(f - x)^2) + best_{r-1}
+//    from the stored row with the same fp32 operations as the forward step,
+//    and takes their lexicographic (cost, w) minimum: the first-index argmin
+//    the forward pass would have recorded.
+//  * The traceback is a small state machine in shared memory that a 17th
+//    warp (the "job warp", threads kVT .. kVT + 31) runs during a forward pass
+//    of ANOTHER tile.  The 16 forward warps synchronise their steps on a named
+//    barrier of their own, so the job warp never waits for them nor they for
+//    it: it reads only completed rows of its own tile, and its serial latency
+//    (fetch, cost, warp reduction per row) stays off the forward critical
+//    path.  The two meet again at the end of the pass.  A CTA
+//    therefore keeps two tiles in
+//    flight and runs them in four phases per pair (F = forward pass, T =
+//    traceback; pass 2 needs pass 1's traceback, the write-back needs pass 2's):
+//        F1(A) | T2(previous B)
+//        F1(B) | T1(A)
+//        F2(A) | T1(B)
+//        F2(B) | T2(A)
+//    A phase ends when both its forward pass and its traceback are done.
+//  * K = 2, 3 keep the tracked encoder: their rows (64 / 32 KB per step) would
+//    cost more HBM traffic than the argmin tracking they save.
+#pragma once
+#include "viterbi.cuh"
+
+namespace exl3b {
+
+constexpr int kLazyThreads = kVT + 32;   // 16 forward warps + the job warp
+
+template <int K>
+struct Lazy {
+    using G = Geo<K>;
+    static constexpr int ROWS = kSteps - 1;                       // rows 1..254 used
+    static constexpr size_t REGION = (size_t)ROWS * G::SPRE * 4;  // bytes per tile region
+    static constexpr int NPL = G::NC > 32 ? G::NC / 32 : 1;       // candidates per lane
+};
+
+// Traceback job state (shared memory; read by all lanes of the job warp,
+// written by its lane 0).  r: the next row to resolve (s = s_r known); rows r-1 .. stop are
+// read; the job ends with s = s_stop.
+struct TbJob {
+    const float* rows;   // this tile's row region
+    int slot;            // pipeline slot of the tile (its xs / st)
+    int want_states;     // pass 2: write every state into st[slot]
+    int rol;             // roll of the pass (x of step i = xs[(i - rol) & 255])
+    int overlap;         // best_0 = 0 at `overlap` (or everywhere if < 0), +inf elsewhere
+    int stop;
+    int r;
+    int s;
+    int pending;         // unused
+    int active;
+    int result;          // s_stop once done
+    int pad;
+};
+
+// Shared memory of a lazy-pipeline CTA.
+template <int K>
+struct LazySmem {
+    using G = Geo<K>;
+    static constexpr int B_BYTES = VitSmem<K>::B_BYTES;
+    static constexpr int OFF_B0 = 0;
+    static constexpr int OFF_B1 = B_BYTES;
+    static constexpr int OFF_X = 2 * B_BYTES;             // xs[2][256] fp32
+    static constexpr int OFF_ST = OFF_X + 2048;           // st[2][256] int32
+    static constexpr int OFF_RED = OFF_ST + 2048;         // reductions, broadcast words
+    static constexpr int OFF_JOB = OFF_RED + 256;         // TbJob
+    static constexpr int OFF_EXTRA = OFF_JOB + 64;        // caller-owned tail
+    static constexpr int BYTES = OFF_EXTRA;
+};
+
+// Run the armed traceback job to its end (the job warp; every lane calls it;
+// job state in registers).  Per row r (s = s_r known; group j = s >> K): lane
+// w (and w + 32, ... for K >= 6) loads best_{r-1}[(j >> K) + w P] (L2-coherent:
+// the rows were written by other warps) and the decode value of predecessor
+// j + w 2^(16-K), forms the forward step's cost fl(fl(f - x)^2) + best, and
+// the warp takes the lexicographic (cost, w) minimum with two redux.sync
+// minima (costs are >= +0 or +inf, so their bit patterns order like the
+// floats).  s_{r-1} = j + w* 2^(16-K).  Ends with jb->result = s_stop.
+template <int K>
+__device__ __forceinline__ void tb_job_run(char* smem, const float* __restrict__ lut32,
+                                           int lane) {
+    using G = Geo<K>;
+    using SM = LazySmem<K>;
+    volatile TbJob* jb = reinterpret_cast<volatile TbJob*>(smem + SM::OFF_JOB);
+    if (!jb->active) return;
+    const float* rows = jb->rows;
+    const int slot = jb->slot;
+    const bool want = jb->want_states != 0;
+    const int rol = jb->rol;
+    const int overlap = jb->overlap;
+    const int stop = jb->stop;
+    int r = jb->r;
+    int s = jb->s;
+    __syncwarp();
+    const float* xs = reinterpret_cast<const float*>(smem + SM::OFF_X) + 256 * slot;
+    int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST) + 256 * slot;
+    const float INF = __int_as_float(0x7f800000);
+    for (; r > stop; --r) {
+        const int j = s >> K;
+        const int m = j >> K;
+        const int q = r - 1;
+        const float* row = rows + (size_t)q * G::SPRE;
+        const float x = xs[(q - rol) & 255];
+        uint32_t kc = 0xFFFFFFFFu;      // this lane's best cost bits, first index
+        uint32_t kw = 0xFFFFFFFFu;
+#pragma unroll
+        for (int k = 0; k < Lazy<K>::NPL; ++k) {
+            const int w = lane + 32 * k;
+            if (w < G::NC) {
+                const int idx = m + w * G::P;
+                const float b = (q == 0) ? ((overlap < 0 || idx == overlap) ? 0.0f : INF)
+                                         : __ldcg(row + idx);
+                const float d = __fsub_rn(__ldg(lut32 + j + (w << (16 - K))), x);
+                const uint32_t c = __float_as_uint(__fadd_rn(__fmul_rn(d, d), b));
+                if (c < kc) { kc = c; kw = (uint32_t)w; }
+            }
+        }
+        const uint32_t cmin = __reduce_min_sync(0xffffffffu, kc);
+        const uint32_t wmin = __reduce_min_sync(0xffffffffu, kc == cmin ? kw : 0xFFFFFFFFu);
+        s = j + ((int)wmin << (16 - K));
+        if (want && lane == 0) st[q] = s;
+    }
+    __syncwarp();
+    if (lane == 0) {
+        jb->r = r;
+        jb->s = s;
+        jb->active = 0;
+        jb->result = s;
+    }
+    __syncwarp();
+}
+
+// The job warp runs the job to its end; then the whole CTA synchronises.
+template <int K>
+__device__ __forceinline__ void tb_job_drain(char* smem, const float* __restrict__ lut32,
+                                             int t) {
+    if (t >= kVT) tb_job_run<K>(smem, lut32, t - kVT);
+    __syncthreads();
+}
+
+// Arm the job (thread 0; the caller synchronises before the next pass).
+template <int K>
+__device__ __forceinline__ void tb_job_start(char* smem, const float* rows, int slot,
+                                             int want_states, int rol, int overlap, int stop,
+                                             int r, int s) {
+    using SM = LazySmem<K>;
+    TbJob* jb = reinterpret_cast<TbJob*>(smem + SM::OFF_JOB);
+    jb->rows = rows;
+    jb->slot = slot;
+    jb->want_states = want_states;
+    jb->rol = rol;
+    jb->overlap = overlap;
+    jb->stop = stop;
+    jb->r = r;
+    jb->s = s;
+    jb->pending = 0;
+    jb->active = 1;
+    jb->result = s;
+}
+
+// One forward pass of the tile in pipeline slot `slot` (targets xs[slot]):
+// untraced steps that store best_q for q in [max(stop, 1), nsteps - 2] to
+// `rows`, then the traced final step and the first-index argmin over the end
+// states (pass 2: restricted to group `overlap`).  Threads 0 .. kVT-1 run the
+// trellis (named barrier 1 between steps); the job warp runs the armed
+// traceback job (if any) meanwhile.  Every thread of the CTA (kLazyThreads)
+// calls it; both the pass and the job are complete on return.  Returns
+// s_{nsteps-1}, and when `st_last` is set stores it there.
+template <int K>
+__device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, int slot,
+                                         int rol, int nsteps, int overlap, int stop,
+                                         float* __restrict__ rows, int32_t* st_last,
+                                         const float* __restrict__ lut32, int t) {
+    using G = Geo<K>;
+    using SM = LazySmem<K>;
+    float* Bc = reinterpret_cast<float*>(smem + SM::OFF_B0);
+    float* Bn = reinterpret_cast<float*>(smem + SM::OFF_B1);
+    const float* xs = reinterpret_cast<const float*>(smem + SM::OFF_X) + 256 * slot;
+    float* redc = reinterpret_cast<float*>(smem + SM::OFF_RED);
+    int* reds = reinterpret_cast<int*>(smem + SM::OFF_RED + 64);
+    int* bcast = reinterpret_cast<int*>(smem + SM::OFF_RED + 128);
+    float* zword = reinterpret_cast<float*>(smem + SM::OFF_RED + 192);
+    const float INF = __int_as_float(0x7f800000);
+    if (t == 0) *zword = 0.0f;
+    if (t < kVT)
+        for (int idx = t; idx < G::SPRE; idx += kVT)
+            Bc[G::baddr(idx)] = (overlap < 0 || idx == overlap) ? 0.0f : INF;
+    __syncthreads();
+    float zr;
+    asm volatile("ld.volatile.shared.f32 %0, [%1];" : "=f"(zr)
+                 : "r"((uint32_t)__cvta_generic_to_shared(zword)));
+
+    const int lo = max(stop, 1);
+    if (t < kVT) {
+        for (int i = 0; i < nsteps - 1; ++i) {
+            const float x = xs[(i - rol) & 255];
+            float* grow = (i + 1 >= lo) ? rows + (size_t)(i + 1) * G::SPRE : nullptr;
+            vit_step<K, false>(f2, x, Bc, Bn, t, zr, grow);
+            float* tmp = Bc; Bc = Bn; Bn = tmp;
+            asm volatile("bar.sync 1, %0;" :: "r"(kVT) : "memory");
+        }
+        // final step, traced: first-index argmin over cost_{n-1} (see vit_pass)
+        const float x = xs[(nsteps - 1 - rol) & 255];
+        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t, zr);
+        float bc = INF;
+        int bs = 0x7fffffff;
+#pragma unroll
+        for (int e = 0; e < G::NOUT; ++e) {
+            const int j = G::out_j(t, e);
+            float v = Bn[G::baddr(j)];
+            if (overlap >= 0 && j != overlap) v = INF;
+            const int w = (int)((bits >> (e * G::BPE)) & ((1u << G::BPE) - 1u));
+            lex_min(bc, bs, v, j + (w << (16 - K)));
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float oc = __shfl_xor_sync(0xffffffffu, bc, off);
+            const int os = __shfl_xor_sync(0xffffffffu, bs, off);
+            lex_min(bc, bs, oc, os);
+        }
+        if ((t & 31) == 0) { redc[t >> 5] = bc; reds[t >> 5] = bs; }
+    } else {
+        tb_job_run<K>(smem, lut32, t - kVT);
+    }
+    __syncthreads();
+    if (t == 0) {
+        float bc = redc[0];
+        int s = reds[0];
+        for (int wv = 1; wv < kVT / 32; ++wv) lex_min(bc, s, redc[wv], reds[wv]);
+        *bcast = s;
+        if (st_last) *st_last = s;
+    }
+    __syncthreads();
+    const int out = *bcast;
+    __syncthreads();
+    return out;
+}
+
+}  // namespace exl3b

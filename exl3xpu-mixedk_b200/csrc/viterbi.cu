@@ -9,10 +9,17 @@
 // across the sequence loop); one sequence per CTA keeps the encoder
 // spill-free.
 #include "exl3b_internal.h"
+#include "vit_lazy.cuh"
 #include "viterbi.cuh"
 
 namespace exl3b {
 
+// Batches of at least two sequences per SM at K >= 4 go through the lazy-argmin
+// pipeline instead (vit_lazy.cuh): SM-count persistent CTAs, CTA b encoding
+// sequences b, b + grid, b + 2 grid, ... two at a time, with two row regions of
+// the workspace (Lazy<K>::REGION bytes each).  Its loop state lives in shared
+// memory, not in registers.
+//
 // One CTA of kVT threads writes the pre-paired decode words of every thread.
 template <int K>
 __global__ void __launch_bounds__(kVT)
@@ -69,6 +76,90 @@ tailbite_kernel(const float* __restrict__ X, int pivot, int margin,
             reinterpret_cast<const int32_t*>(smem + SM::OFF_ST)[t];
 }
 
+
+template <int K>
+__global__ void __launch_bounds__(kLazyThreads, 1)
+tailbite_lazy_kernel(const float* __restrict__ X, int nseq, int pivot, int margin,
+                     int32_t* __restrict__ states, float* __restrict__ regions,
+                     const uint4* __restrict__ f2tab, const float* __restrict__ lut32) {
+    extern __shared__ __align__(16) char smem[];
+    using SM = LazySmem<K>;
+    using L = Lazy<K>;
+    const int t = threadIdx.x;
+    __half2 f2[64];
+    vit_load_f2tab(f2, f2tab, t < kVT ? t : 0);
+    float* xs = reinterpret_cast<float*>(smem + SM::OFF_X);
+    int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST);
+    volatile TbJob* jb = reinterpret_cast<volatile TbJob*>(smem + SM::OFF_JOB);
+    // pending pass-2 traceback of the previous pair's B: have, seq, s_pivot, s_255
+    volatile int* ctl = reinterpret_cast<volatile int*>(smem + SM::OFF_RED + 224);
+    float* reg0 = regions + (size_t)(2 * blockIdx.x) * (L::REGION / 4);
+    float* reg1 = reg0 + L::REGION / 4;
+    const int n1 = (margin > 0 && pivot + margin < kSteps) ? pivot + margin : kSteps;
+    const int nmine = nseq > (int)blockIdx.x ? (nseq - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    if (t == 0) {
+        jb->active = 0;
+        ctl[0] = 0;
+    }
+    __syncthreads();
+    for (int k = 0; k < nmine; k += 2) {
+        const int seqA = blockIdx.x + k * gridDim.x;
+        const bool hasB = k + 1 < nmine;
+        // ---- phase a: F1(A) | T2(previous B)
+        if (t < 64)
+            reinterpret_cast<float4*>(xs)[t] =
+                reinterpret_cast<const float4*>(X + (size_t)seqA * kSteps)[t];
+        if (t == 0 && ctl[0])
+            tb_job_start<K>(smem, reg1, 1, 1, 0, ctl[2] >> K, 0, kSteps - 1, ctl[3]);
+        __syncthreads();
+        const int fA1 = lazy_pass<K>(f2, smem, 0, pivot, n1, -1, pivot, reg0, nullptr, lut32, t);
+        tb_job_drain<K>(smem, lut32, t);
+        if (ctl[0] && t < kSteps) states[(size_t)ctl[1] * kSteps + t] = st[kSteps + t];
+        __syncthreads();
+        // ---- phase b: F1(B) | T1(A)
+        if (hasB && t < 64)
+            reinterpret_cast<float4*>(xs + kSteps)[t] =
+                reinterpret_cast<const float4*>(X + (size_t)(seqA + gridDim.x) * kSteps)[t];
+        if (t == 0) tb_job_start<K>(smem, reg0, 0, 0, pivot, -1, pivot, n1 - 1, fA1);
+        __syncthreads();
+        int fB1 = 0;
+        if (hasB) fB1 = lazy_pass<K>(f2, smem, 1, pivot, n1, -1, pivot, reg1, nullptr, lut32, t);
+        tb_job_drain<K>(smem, lut32, t);
+        const int spA = jb->result;
+        __syncthreads();
+        // ---- phase c: F2(A) | T1(B)
+        if (hasB && t == 0) tb_job_start<K>(smem, reg1, 1, 0, pivot, -1, pivot, n1 - 1, fB1);
+        __syncthreads();
+        const int fA2 = lazy_pass<K>(f2, smem, 0, 0, kSteps, spA >> K, 0, reg0, &st[kSteps - 1],
+                                     lut32, t);
+        tb_job_drain<K>(smem, lut32, t);
+        const int spB = hasB ? jb->result : 0;
+        __syncthreads();
+        // ---- phase d: F2(B) | T2(A)
+        if (t == 0) tb_job_start<K>(smem, reg0, 0, 1, 0, spA >> K, 0, kSteps - 1, fA2);
+        __syncthreads();
+        int fB2 = 0;
+        if (hasB)
+            fB2 = lazy_pass<K>(f2, smem, 1, 0, kSteps, spB >> K, 0, reg1, &st[2 * kSteps - 1],
+                               lut32, t);
+        tb_job_drain<K>(smem, lut32, t);
+        if (t < kSteps) states[(size_t)seqA * kSteps + t] = st[t];
+        if (t == 0) {
+            ctl[0] = hasB ? 1 : 0;
+            ctl[1] = seqA + gridDim.x;
+            ctl[2] = spB;
+            ctl[3] = fB2;
+        }
+        __syncthreads();
+    }
+    if (ctl[0]) {
+        if (t == 0) tb_job_start<K>(smem, reg1, 1, 1, 0, ctl[2] >> K, 0, kSteps - 1, ctl[3]);
+        __syncthreads();
+        tb_job_drain<K>(smem, lut32, t);
+        if (t < kSteps) states[(size_t)ctl[1] * kSteps + t] = st[kSteps + t];
+    }
+}
+
 size_t bp_slot_bytes(int K) {
     switch (K) {
         case 2: return (size_t)kSteps * Geo<2>::BP_ROW;
@@ -110,9 +201,61 @@ static int launch_k(const float* dX, int nseq, int pivot, int margin,
     return RC_OK;
 }
 
+template <int K>
+static int launch_lazy_k(const float* dX, int nseq, int pivot, int margin, int32_t* dStates,
+                         uint8_t* ws, int grid, const uint4* f2tab, const float* lut32,
+                         cudaStream_t stream) {
+    const int smem = LazySmem<K>::BYTES;
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev]) {
+        if (check_cuda(cudaFuncSetAttribute(tailbite_lazy_kernel<K>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                       "cudaFuncSetAttribute(tailbite_lazy)"))
+            return RC_DEVICE_ERROR;
+        attr_set[dev] = true;
+    }
+    prof_begin_launch(stream, PROF_TAILBITE, (double)nseq * kSteps);
+    tailbite_lazy_kernel<K><<<grid, kLazyThreads, smem, stream>>>(
+        dX, nseq, pivot, margin, dStates, reinterpret_cast<float*>(ws), f2tab, lut32);
+    prof_end_launch(stream);
+    note_launch();
+    return check_cuda(cudaGetLastError(), "tailbite_lazy_kernel launch") ? RC_DEVICE_ERROR
+                                                                       : RC_OK;
+}
+
+size_t lazy_region_bytes(int K) {
+    switch (K) {
+        case 4: return Lazy<4>::REGION;
+        case 5: return Lazy<5>::REGION;
+        case 6: return Lazy<6>::REGION;
+        case 7: return Lazy<7>::REGION;
+    }
+    return 0;
+}
+
+TailbitePlan tailbite_plan(int nseq, int K, int sms) {
+    TailbitePlan p;
+    p.lazy = K >= 4 && sms > 0 && nseq >= 2 * sms;
+    p.grid = p.lazy ? sms : (nseq < sms ? nseq : sms);
+    p.bytes = p.lazy ? (size_t)p.grid * 2 * lazy_region_bytes(K)
+                     : (size_t)p.grid * bp_slot_bytes(K);
+    return p;
+}
+
 int launch_tailbite(const float* dX, int nseq, int K, int pivot, int margin,
-                    int32_t* dStates, uint8_t* ws, int grid,
-                    const uint4* f2tab, cudaStream_t stream) {
+                    int32_t* dStates, uint8_t* ws, const TailbitePlan& plan,
+                    const uint4* f2tab, const float* lut32, cudaStream_t stream) {
+    const int grid = plan.grid;
+    if (plan.lazy) {
+        switch (K) {
+            case 4: return launch_lazy_k<4>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
+            case 5: return launch_lazy_k<5>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
+            case 6: return launch_lazy_k<6>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
+            case 7: return launch_lazy_k<7>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
+        }
+    }
     switch (K) {
         case 2: return launch_k<2>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
         case 3: return launch_k<3>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, stream);
