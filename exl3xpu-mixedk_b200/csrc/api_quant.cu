@@ -255,7 +255,8 @@ int exl3b_u_to_gram(const float* dU, int k, double* dG, void* ws, size_t ws_byte
 
 // ------------------------------------------------------------------ LDLQ
 // Workspace: E [k][n] | prod [k][n] (LDLQ only) | backpointer slots |
-// control words (slot flags, per-column progress, ticket, error word).
+// control words (slot flags, per-column progress, ticket, error word) |
+// lazy-pipeline row regions (SMs x 2 x Lazy<K>::REGION, largest for K = 4).
 static int sweep_slots() { return device_sms() * ldlq_tile_max_resident_per_sm() + 16; }
 
 static size_t sweep_slot(const int* seg_K, int nseg) {
@@ -271,12 +272,16 @@ static size_t sweep_ctrl_bytes(int tn) {
     return align256(((size_t)sweep_slots() + (size_t)tn + 24) * sizeof(int));
 }
 
+static size_t sweep_lazy_bytes(int kmin) {
+    return align256((size_t)device_sms() * 2 * lazy_region_bytes(kmin > 4 ? kmin : 4));
+}
+
 size_t exl3b_ldlq_workspace_bytes(int k, int n, int kmin, int use_ldlq) {
     if (k <= 0 || n <= 0 || k % 16 || n % 16 || kmin < 2 || kmin > 7) return 0;
     const size_t kn = (size_t)k * n * 4;
     const size_t bp = (size_t)sweep_slots() * bp_slot_bytes(kmin);
     return align256(kn) + (use_ldlq ? align256(kn) : 0) + align256(bp) +
-           sweep_ctrl_bytes(n / 16);
+           sweep_ctrl_bytes(n / 16) + sweep_lazy_bytes(kmin);
 }
 
 int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nseg,
@@ -338,6 +343,7 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     a.bp_ws = w;
     w += align256((size_t)a.nslots * bp_slot_bytes(kmin));
     int* ctrl = reinterpret_cast<int*>(w);
+    a.lazy_ws = reinterpret_cast<float*>(w + sweep_ctrl_bytes(tn));
     a.slots = ctrl;
     a.colprog = ctrl + a.nslots;
     a.tickets = a.colprog + tn;

@@ -131,6 +131,7 @@ struct SweepArgs {
     float* xout;
     uint8_t* bp_ws;
     size_t bp_slot;
+    float* lazy_ws;          // lazy pipeline: SMs x 2 row regions (K >= 4 launches)
     int nslots;              // backpointer slots (> SM count)
     int* slots;              // [nslots] ownership flags (zero at sweep start)
     int* colprog;            // [tn] finished k-blocks per column (zero at start)

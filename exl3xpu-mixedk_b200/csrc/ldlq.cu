@@ -11,7 +11,9 @@
 //
 // Sweep (host loop, all launches on one stream): k-blocks right to left in
 // 128-row buffers.  One tile-kernel launch per buffer covers all its k-blocks x
-// column tiles: each CTA takes a ticket in dependency order (k-block
+// column tiles.  K >= 4 launches with at least two tiles per SM use the
+// persistent lazy-argmin kernel (ldlq_lazy.cu); the others, one CTA per tile
+// with the traced encoder, below.  Each CTA takes a ticket in dependency order (k-block
 // descending, column ascending) and, when it needs the block below it in the
 // same column (intra-buffer feedback), waits on that column's progress
 // counter.  The producer of that block took an earlier ticket, so it is
@@ -29,52 +31,10 @@
 #include <string.h>
 
 #include "exl3b_internal.h"
+#include "ldlq_tile.cuh"
 #include "viterbi.cuh"
 
 namespace exl3b {
-
-constexpr int kMaxSeg = 8;
-
-struct LdlqTileParams {
-    const float* Wq;
-    float* E;
-    float* hatW;
-    const float* Lfac;      // null: no feedback
-    const float* prod;      // null: no feedback
-    int k, n;
-    int cur;                // buffer end block (exclusive)
-    int top;                // first (highest) k-block of this launch
-    int tk;                 // k-blocks of the whole matrix
-    int pivot, margin;
-    int* tickets;           // launch ticket counter (zeroed before launch)
-    int* colprog;           // [tn] k-blocks finished per column (sweep-wide)
-    int* slots;             // [nslots] backpointer-slot ownership flags
-    int nslots;
-    int* err;               // error word (set on a wait time-out)
-    int nseg;
-    int seg_c0[kMaxSeg + 1];     // segment column-tile starts, seg_c0[nseg] = tn
-    int seg_K[kMaxSeg];
-    int16_t* seg_trellis[kMaxSeg];
-    // segments encoded by this launch (all of one K): ids and column prefix
-    int nls;
-    int ls_seg[kMaxSeg];
-    int ls_pre[kMaxSeg + 1];     // ls_pre[m] = columns of segments ls_seg[0..m)
-    int32_t* states;        // [tk][tn][256] or null
-    float* xout;            // [tk][tn][256] or null (encoder targets, for checks)
-    uint8_t* bp_ws;         // wave slots
-    size_t bp_slot;         // bytes per slot
-    const uint4* f2tab[8];  // per K
-    const float* lut32;     // decode table fp32 [65536]
-};
-
-// sequence step t -> row-major position in the 16x16 tile (quantize.py:101-118)
-__device__ __forceinline__ int tc_perm(int t) {
-    const int tt = t >> 3, q = t & 7;
-    const int r0 = (tt & 3) * 2, c0 = tt >> 2;
-    const int row = r0 + (q & 1) + ((q & 2) ? 8 : 0);
-    const int col = c0 + ((q & 4) ? 8 : 0);
-    return row * 16 + col;
-}
 
 // sched (shared): [0] k-block i, [1] column tile c, [2] backpointer slot,
 // [3] ok, [4] column segment.  Re-read where needed instead of being kept
@@ -82,44 +42,11 @@ __device__ __forceinline__ int tc_perm(int t) {
 template <int K>
 __device__ __forceinline__ void ldlq_tile_body(const LdlqTileParams& p, char* smem,
                                                const volatile int* sched) {
-    int i = sched[0], c = sched[1], seg;
     using SM = VitSmem<K>;
     const int t = threadIdx.x;
     float* xs = reinterpret_cast<float*>(smem + SM::OFF_X);
     float* wx = reinterpret_cast<float*>(smem + SM::OFF_TB);   // 16x16 staging
-    const int tn = p.seg_c0[p.nseg];
-    const size_t n = (size_t)p.n;
-
-    // ---- feedback: WXWX tile
-    if (t < 256) {
-        const int a = t >> 4, col = t & 15;
-        const size_t row = (size_t)(16 * i + a);
-        const size_t gc = (size_t)(16 * c + col);
-        float w = p.Wq[row * n + gc];
-        if (p.Lfac) {
-            const int r_lo = 16 * (i + 1), r_hi = 16 * p.cur;
-            if (r_lo < r_hi) {
-                // E rows of this buffer were written by other CTAs of this
-                // launch: read them at L2 (ld.global.cg), never from a
-                // possibly stale L1 line shared with a neighbouring column
-                float acc = 0.0f;
-                for (int r = r_lo; r < r_hi; ++r)
-                    acc = fmaf(p.Lfac[(size_t)r * p.k + 16 * i + a],
-                               __ldcg(&p.E[(size_t)r * n + gc]), acc);
-                w = w + acc;
-            }
-            w = w + p.prod[row * n + gc];
-        }
-        wx[t] = w;
-    }
-    __syncthreads();
-    if (t < 256) {
-        const float x = wx[tc_perm(t)];
-        xs[t] = x;
-        if (p.xout) p.xout[((size_t)i * tn + c) * 256 + t] = x;
-    }
-    __syncthreads();
-
+    tile_feedback_gather(p, sched[0], sched[1], xs, wx, t);
     // ---- trellis encode
     {
         __half2 f2[64];
@@ -127,51 +54,11 @@ __device__ __forceinline__ void ldlq_tile_body(const LdlqTileParams& p, char* sm
         uint8_t* bp = p.bp_ws + (size_t)sched[2] * p.bp_slot;
         vit_tailbite<K>(f2, smem, p.pivot, p.margin, bp, t);
     }
-
-    // ---- write-back: decoded tile, error, states.  The column tile and its
-    // segment are recomputed from the launch parameters here rather than kept
-    // live in registers across the encode.
-    i = sched[0];
-    c = sched[1];
-    seg = sched[4];
-    const int32_t* st = reinterpret_cast<const int32_t*>(smem + SM::OFF_ST);
-    if (t < 256) {
-        const int s = st[t];
-        const int pos = tc_perm(t);
-        const size_t idx = (size_t)(16 * i + (pos >> 4)) * n + (size_t)(16 * c + (pos & 15));
-        const float v = p.lut32[s];
-        p.hatW[idx] = v;
-        p.E[idx] = p.Wq[idx] - v;
-        if (p.states) p.states[((size_t)i * tn + c) * 256 + t] = s;
-    }
-    // ---- pack: stream bit q = t*K + b (MSB first within a symbol); u32 word
-    // w holds stream bits [32w, 32w+32) MSB first; stored as int16 low half
-    // first (quantize.py:360-378)
-    constexpr int NW = 8 * K;
-    if (t < NW) {
-        uint32_t word = 0;
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j) {
-            const int q = 32 * t + j;
-            const int step = q / K, b = q - step * K;
-            const uint32_t bit = ((uint32_t)st[step] >> (K - 1 - b)) & 1u;
-            word |= bit << (31 - j);
-        }
-        const int seg_tn = p.seg_c0[seg + 1] - p.seg_c0[seg];
-        int16_t* out = p.seg_trellis[seg] +
-                       ((size_t)i * seg_tn + (c - p.seg_c0[seg])) * (16 * K);
-        out[2 * t] = (int16_t)(word & 0xFFFFu);
-        out[2 * t + 1] = (int16_t)(word >> 16);
-    }
+    // ---- write-back: the column tile and its segment are re-read from shared
+    // memory here rather than kept live in registers across the encode.
+    tile_writeback<K>(p, sched[0], sched[1], sched[4],
+                      reinterpret_cast<const int32_t*>(smem + SM::OFF_ST), t);
 }
-
-__device__ __forceinline__ int ld_acquire(const int* p) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-constexpr long long kWaitNs = 4000000000LL;   // 4 s bound on any dependency wait
 
 // slot-holder tag: (SM id << 20) | (ticket + 1), nonzero
 __device__ __forceinline__ int holder_tag(int ticket) {
@@ -187,14 +74,9 @@ ldlq_tile_kernel(const __grid_constant__ LdlqTileParams p) {
     __shared__ int sched[5];            // i, c, slot, ok, segment
     const int t = threadIdx.x;
     if (t == 0) {
-        const int ncols = p.ls_pre[p.nls];
         const int ticket = atomicAdd(p.tickets, 1);
-        const int i = p.top - ticket / ncols;
-        const int lc = ticket % ncols;
-        int m = 0;
-        while (m + 1 < p.nls && lc >= p.ls_pre[m + 1]) ++m;
-        const int seg = p.ls_seg[m];
-        const int c = p.seg_c0[seg] + (lc - p.ls_pre[m]);
+        int i, c, seg;
+        tile_of_ticket(p, ticket, i, c, seg);
         int ok = 1;
         // backpointer slot: nslots exceeds the CTAs the device can hold
         // resident at once (SMs x occupancy), so at every instant a slot is
@@ -330,6 +212,8 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
     for (int s = 0; s <= a.nseg; ++s) p.seg_c0[s] = a.seg_c0[s];
     for (int s = 0; s < a.nseg; ++s) { p.seg_K[s] = a.seg_K[s]; p.seg_trellis[s] = a.seg_trellis[s]; }
     p.states = a.states; p.xout = a.xout; p.bp_ws = a.bp_ws; p.bp_slot = a.bp_slot;
+    p.lazy_ws = a.lazy_ws;
+    const int sms = device_sms();
     p.slots = a.slots; p.nslots = a.nslots; p.colprog = a.colprog; p.err = a.err;
     for (int K = 0; K < 8; ++K) p.f2tab[K] = a.f2tab[K];
     p.lut32 = a.lut32;
@@ -356,8 +240,12 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
             if (check_cuda(cudaMemsetAsync(a.tickets, 0, sizeof(int), stream), "memset tickets"))
                 return RC_DEVICE_ERROR;
             const long long nb = (long long)(hi - lo) * p.ls_pre[p.nls];
+            p.ntiles = (int)nb;
             prof_begin_launch(stream, PROF_TILE, (double)nb * 256.0);
-            const int rc = launch_tile(K, p, (unsigned)nb, stream);
+            // K >= 4 with at least two tiles per SM: persistent CTAs, lazy argmin
+            const bool lazy = K >= 4 && a.lazy_ws != nullptr && sms > 0 && nb >= 2LL * sms;
+            const int rc = lazy ? launch_lazy_tile(K, p, (unsigned)sms, stream)
+                                : launch_tile(K, p, (unsigned)nb, stream);
             prof_end_launch(stream);
             if (rc) return rc;
         }

@@ -313,3 +313,32 @@ def test_stored_fields_dequantise_to_w_hat(xq, tmp_path):
         else:
             rel = (w - r["W_hat"]).abs().max() / r["W_hat"].abs().max()
             assert rel <= 1e-3, rel
+
+
+@pytest.mark.parametrize("k,n,K,buf_cols,pivot,margin", [
+    (256, 768, 4, 128, 128, 0),      # 8 x 48 = 384 tiles per buffer launch
+    (256, 640, 5, 128, 7, 16),       # short first pass
+    (256, 1184, 7, 128, 200, 100),
+    (2560, 160, 6, 1024, 128, 0),    # 10 columns, 64-block buffers: a CTA's own
+                                     # pending tiles are often a new tile's dependency
+    (4864, 16, 4, 4864, 128, 0),     # one column: every B depends on its A
+])
+def test_lazy_sweep_dual_check(xq, oracle, mul1_lut, k, n, K, buf_cols, pivot, margin):
+    """Buffer launches of >= 2 tiles per SM at K >= 4 run the persistent
+    lazy-argmin tile kernel: every k-block's encoder targets, re-encoded by the
+    CPU oracle, give the sweep's states (the reference's per-launch dual
+    check), and the trellis decodes to hatW."""
+    from exl3b import api
+    W, H = _ldlq_problem(k, 16, 50 + K)
+    dev = torch.device("cuda", 0)
+    Lfac = api._damped_lfac(H, xq.sign_vec(k, 9).half(), 0.01, dev)
+    Wq = torch.randn(k, n, generator=torch.Generator().manual_seed(60 + K)).to(dev)
+    hatW, trl, st, X = api._sweep(Wq, Lfac, [K], [n], "exl3_mul1", pivot, margin, buf_cols,
+                                  want_states=True, want_x=True)
+    Xh, sth = X.cpu().numpy(), st.cpu().numpy()
+    ref = oracle.tailbite(Xh.reshape(-1, 256), mul1_lut, K, pivot=pivot, margin=margin,
+                          nthreads=NTH)
+    bad = np.nonzero((ref != sth.reshape(-1, 256)).any(1))[0]
+    assert bad.size == 0, f"{bad.size} tiles differ, first {bad[:5]}"
+    lut = xq.get_lut("exl3_mul1").to(dev)
+    assert torch.equal(xq.decode_trellis(trl[0], lut, K, k, n), hatW)
