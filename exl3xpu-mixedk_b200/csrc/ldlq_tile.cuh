@@ -123,7 +123,7 @@ __device__ __forceinline__ void tile_writeback(const LdlqTileParams& p, int i, i
     const int tn = p.seg_c0[p.nseg];
     const size_t n = (size_t)p.n;
     if (t < 256) {
-        const int s = st[t];
+        const int s = st[t] & 0xFFFF;        // states are 16-bit
         const int pos = tc_perm(t);
         const size_t idx = (size_t)(16 * i + (pos >> 4)) * n + (size_t)(16 * c + (pos & 15));
         const float v = p.lut32[s];

@@ -8,8 +8,9 @@
 //    predecessor pair -- about half the work of tracking the argmin), and each
 //    thread streams its outputs best_{i+1}[j] of every step the traceback will
 //    cross to a per-tile row region in global memory (natural index order,
-//    row q = best_q).  Only the last step of a pass tracks its argmin (the
-//    final first-index argmin of the pass).
+//    row q = best_q).  The end state of a pass (the first-index argmin over
+//    the last step's costs) is found by rescanning only the group(s) that
+//    reach the minimum.
 //  * The traceback recomputes, for the one group j = s >> K on the path, the
 //    2^K candidate costs cost_{r-1}(j + w 2^(16-K)) = fl(fl(f - x)^2) + best_{r-1}
 //    from the stored row with the same fp32 operations as the forward step,
@@ -108,7 +109,7 @@ __device__ __forceinline__ void tb_job_run(char* smem, const float* __restrict__
     int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST) + 256 * slot;
     const float INF = __int_as_float(0x7f800000);
     for (; r > stop; --r) {
-        const int j = s >> K;
+        const int j = (s & 0xFFFF) >> K;      // states are 16-bit
         const int m = j >> K;
         const int q = r - 1;
         const float* row = rows + (size_t)q * G::SPRE;
@@ -172,8 +173,8 @@ __device__ __forceinline__ void tb_job_start(char* smem, const float* rows, int 
 
 // One forward pass of the tile in pipeline slot `slot` (targets xs[slot]):
 // untraced steps that store best_q for q in [max(stop, 1), nsteps - 2] to
-// `rows`, then the traced final step and the first-index argmin over the end
-// states (pass 2: restricted to group `overlap`).  Threads 0 .. kVT-1 run the
+// `rows`, then the first-index argmin over the end states (pass 2: restricted
+// to group `overlap`).  Threads 0 .. kVT-1 run the
 // trellis (named barrier 1 between steps); the job warp runs the armed
 // traceback job (if any) meanwhile.  Every thread of the CTA (kLazyThreads)
 // calls it; both the pass and the job are complete on return.  Returns
@@ -202,43 +203,66 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
     asm volatile("ld.volatile.shared.f32 %0, [%1];" : "=f"(zr)
                  : "r"((uint32_t)__cvta_generic_to_shared(zword)));
 
-    const int lo = max(stop, 1);
+    // rows the traceback reads: best_q, q in [max(stop, 1), nsteps - 2]
+    const int lo = max(stop, 1), hi = nsteps - 2;
     if (t < kVT) {
         for (int i = 0; i < nsteps - 1; ++i) {
             const float x = xs[(i - rol) & 255];
-            float* grow = (i + 1 >= lo) ? rows + (size_t)(i + 1) * G::SPRE : nullptr;
+            float* grow = (i + 1 >= lo && i + 1 <= hi) ? rows + (size_t)(i + 1) * G::SPRE
+                                                       : nullptr;
             vit_step<K, false>(f2, x, Bc, Bn, t, zr, grow);
             float* tmp = Bc; Bc = Bn; Bn = tmp;
             asm volatile("bar.sync 1, %0;" :: "r"(kVT) : "memory");
         }
-        // final step, traced: first-index argmin over cost_{n-1} (see vit_pass)
+        // final step, untraced: best_n[j] = min_w cost_{n-1}(j + w 2^(16-K)).
+        // The pass ends at the first-index argmin over cost_{n-1}: the lowest
+        // state s = j + w 2^(16-K) whose cost is v* = min_j best_n[j] (pass 2:
+        // only group j == overlap).  Each thread rescans the candidates of its
+        // groups that reach v* (usually one group in the whole CTA) with the
+        // forward step's fp32 operations and takes the group's lexicographic
+        // (cost, w) minimum -- its first-index argmin -- and the CTA the lowest
+        // such state.
         const float x = xs[(nsteps - 1 - rol) & 255];
-        const uint64_t bits = vit_step<K>(f2, x, Bc, Bn, t, zr);
-        float bc = INF;
-        int bs = 0x7fffffff;
+        vit_step<K, false>(f2, x, Bc, Bn, t, zr);
+        float v = INF;
 #pragma unroll
         for (int e = 0; e < G::NOUT; ++e) {
             const int j = G::out_j(t, e);
-            float v = Bn[G::baddr(j)];
-            if (overlap >= 0 && j != overlap) v = INF;
-            const int w = (int)((bits >> (e * G::BPE)) & ((1u << G::BPE) - 1u));
-            lex_min(bc, bs, v, j + (w << (16 - K)));
+            if (overlap < 0 || j == overlap) v = fminf(v, Bn[G::baddr(j)]);
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            const float oc = __shfl_xor_sync(0xffffffffu, bc, off);
-            const int os = __shfl_xor_sync(0xffffffffu, bs, off);
-            lex_min(bc, bs, oc, os);
+        for (int off = 16; off > 0; off >>= 1)
+            v = fminf(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if ((t & 31) == 0) redc[t >> 5] = v;
+        asm volatile("bar.sync 1, %0;" :: "r"(kVT) : "memory");
+        float vs = redc[0];
+        for (int wv = 1; wv < kVT / 32; ++wv) vs = fminf(vs, redc[wv]);
+        int bs = 0x7fffffff;
+        for (int e = 0; e < G::NOUT; ++e) {
+            const int j = G::out_j(t, e);
+            if ((overlap < 0 || j == overlap) && Bn[G::baddr(j)] == vs) {
+                const int m = j >> K;
+                float gc = INF;
+                int gw = 0;
+                for (int w = 0; w < G::NC; ++w) {
+                    const float d = __fsub_rn(lut32[j + (w << (16 - K))], x);
+                    const float c = __fadd_rn(__fmul_rn(d, d), Bc[G::baddr(m + w * G::P)]);
+                    if (c < gc) { gc = c; gw = w; }
+                }
+                bs = min(bs, j + (gw << (16 - K)));
+            }
         }
-        if ((t & 31) == 0) { redc[t >> 5] = bc; reds[t >> 5] = bs; }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+            bs = min(bs, __shfl_xor_sync(0xffffffffu, bs, off));
+        if ((t & 31) == 0) reds[t >> 5] = bs;
     } else {
         tb_job_run<K>(smem, lut32, t - kVT);
     }
     __syncthreads();
     if (t == 0) {
-        float bc = redc[0];
         int s = reds[0];
-        for (int wv = 1; wv < kVT / 32; ++wv) lex_min(bc, s, redc[wv], reds[wv]);
+        for (int wv = 1; wv < kVT / 32; ++wv) s = min(s, reds[wv]);
         *bcast = s;
         if (st_last) *st_last = s;
     }
