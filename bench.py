@@ -419,7 +419,8 @@ def main():
     achieved = w_per_launch * OPS_PER_WEIGHT / (tile_ms_avg / 1e3) / 1e9
     tpw = _profile_traffic()
     roofline = {
-        "kernel": "ldlq_tile_kernel (fused feedback + tail-biting Viterbi + write-back)",
+        "kernel": "LDLQ tile kernel (fused feedback + tail-biting Viterbi + write-back; "
+                  "ldlq_lazy_kernel for K>=4 launches of >= 2 tiles per SM)",
         "bound": "alu", "achieved": achieved, "peak": peak_ops, "unit": "Gop/s",
         "frac": achieved / peak_ops,
         "peak_source": f"{sms} SMs x 128 lanes x {mhz:.0f} MHz (sm_max_mhz of "
