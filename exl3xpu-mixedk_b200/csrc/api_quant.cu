@@ -197,7 +197,9 @@ int exl3b_div_scalar(const float* dx, const float* d_s, float* dy, size_t n, voi
 size_t exl3b_block_ldl_workspace_bytes(int k, int f64) {
     if (k <= 0 || k % 16) return 0;
     const size_t es = f64 ? 8 : 4;
-    return align256((size_t)(k / 16) * 256 * es) + 256;
+    // block inverses | status word | (fp32) transposed panel + GEMM error word
+    return align256((size_t)(k / 16) * 256 * es) + 256 +
+           (f64 ? 0 : align256(ldl_panel_bytes(k)) + 256);
 }
 
 int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
@@ -213,20 +215,35 @@ int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
     uint8_t* w = static_cast<uint8_t*>(ws);
     void* dli = w;
     int* status = reinterpret_cast<int*>(w + align256((size_t)(k / 16) * 256 * es));
+    float* panel = nullptr;
+    int* gerr = nullptr;
+    if (!f64) {
+        panel = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(status) + 256);
+        gerr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(panel) +
+                                      align256(ldl_panel_bytes(k)));
+    }
     cudaStream_t s = S(stream);
-    if (check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "memset status")) return RC_DEVICE_ERROR;
+    if (check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "memset status") ||
+        (gerr && check_cuda(cudaMemsetAsync(gerr, 0, sizeof(int), s), "memset gemm status")))
+        return RC_DEVICE_ERROR;
     prof_begin_launch(s, PROF_LDL, (double)k * k * k / 3.0);
     int rc = f64 ? block_ldl<double>(static_cast<double*>(dA), k, dLfac, static_cast<double*>(dD),
                                      static_cast<double*>(dli), status, s)
                  : block_ldl<float>(static_cast<float*>(dA), k, dLfac, static_cast<float*>(dD),
-                                    static_cast<float*>(dli), status, s);
+                                    static_cast<float*>(dli), status, s, panel, gerr);
     prof_end_launch(s);
     if (rc) return rc;
-    int h = 0;
+    int h = 0, g = 0;
     if (check_cuda(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, s),
                    "read status") ||
+        (gerr && check_cuda(cudaMemcpyAsync(&g, gerr, sizeof(int), cudaMemcpyDeviceToHost, s),
+                            "read gemm status")) ||
         check_cuda(cudaStreamSynchronize(s), "block_ldl sync"))
         return RC_DEVICE_ERROR;
+    if (g) {
+        set_error("block LDL: tensor-core trailing update timed out (%d)", g);
+        return RC_DEVICE_ERROR;
+    }
     if (h) {
         set_error("Cholesky: leading minor of order %d is not positive-definite", h);
         return RC_NOT_SPD;

@@ -12,7 +12,8 @@
 //   * TMA loads 32 x 32 fp32 boxes of A and B (128-byte swizzle) into a staging
 //     buffer, while the previous chunk is being converted / multiplied.
 //   * Each thread takes one M (N) row of the chunk out of staging, splits every
-//     value x into x_hi = tf32(x) and x_lo = tf32(x - x_hi), and writes both
+//     value x (times the sign sa for A) into x_hi = tf32(x) and
+//     x_lo = tf32(x - x_hi), and writes both
 //     into K-major operand tiles in the UMMA 128-byte-swizzle canonical layout
 //     (128-byte rows of 32 k values, 8-row atoms of 1 KB).  The tf32 MMA reads
 //     K-major operands only; the transpose rides on this split pass.
@@ -109,7 +110,7 @@ __device__ __forceinline__ float tf32_round(float x) {
 // per warp (conflict-free); writes are 16-byte chunks whose swizzle spreads 8
 // consecutive rows over all 32 banks.
 __device__ __forceinline__ void split_row(const float* __restrict__ stg, float* __restrict__ hi,
-                                          float* __restrict__ lo, int r) {
+                                          float* __restrict__ lo, int r, float sign) {
     const float* box = stg + (r >> 5) * (kBox / 4);
     const int ml = r & 31;
 #pragma unroll
@@ -118,7 +119,7 @@ __device__ __forceinline__ void split_row(const float* __restrict__ stg, float* 
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int k = 4 * j + e;
-            v[e] = box[k * 32 + ((((ml >> 2) ^ (k & 7))) << 2) + (ml & 3)];
+            v[e] = sign * box[k * 32 + ((((ml >> 2) ^ (k & 7))) << 2) + (ml & 3)];
         }
         float4 h, l;
         h.x = tf32_round(v[0]); l.x = tf32_round(v[0] - h.x);
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(128, 1)
 feedback_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         float* __restrict__ C, int ldc, int M, int N, int K,
-                        int* __restrict__ err) {
+                        float sa, int lower, int* __restrict__ err) {
     extern __shared__ __align__(1024) uint8_t gsm_raw[];
     // 1024-byte alignment for the swizzle atoms
     uint8_t* gsm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
@@ -146,6 +147,8 @@ feedback_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
+    // lower: only tiles that reach the lower triangle (C symmetric update)
+    if (lower && n0 > m0 + kTM - 1) return;
     // bars[0..1]: staging s filled (TMA); bars[2..3]: MMAs reading operand set s done
     const uint32_t bar_full0 = smem_u32(&bars[0]);
     const uint32_t bar_mma0 = smem_u32(&bars[2]);
@@ -196,8 +199,9 @@ feedback_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         if (kc >= 2) commits_done = kc - 1;
         const float* stg = reinterpret_cast<const float*>(stage + s * kStageBytes);
         float* opset = reinterpret_cast<float*>(ops + s * kOpSetBytes);
-        split_row(stg, opset, opset + kOpBytes / 4, t);                         // A rows
-        split_row(stg + kStageBytes / 8, opset + kOpBytes / 2, opset + 3 * kOpBytes / 4, t);  // B rows
+        split_row(stg, opset, opset + kOpBytes / 4, t, sa);                     // A rows
+        split_row(stg + kStageBytes / 8, opset + kOpBytes / 2, opset + 3 * kOpBytes / 4, t,
+                  1.0f);                                                         // B rows
         // generic-proxy shared writes (and the staging reads) before the async
         // proxy (tensor core reads, next TMA write) touches the same memory
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -331,11 +335,14 @@ static int encode_operand(CUtensorMap* map, const float* base, int inner, int ou
     return RC_OK;
 }
 
-// C[M][N] += A_T^T . B on tcgen05 (A_T [K][M], B [K][N], both row-major with
-// leading dimensions lda / ldb; all pointers 16-byte aligned, lda / ldb
-// multiples of 4).  err: device word set to 4 on a barrier time-out.
+// C[M][N] += sa * A_T^T . B on tcgen05 (A_T [K][M], B [K][N], both row-major
+// with leading dimensions lda / ldb; all pointers 16-byte aligned, lda / ldb
+// multiples of 4; sa = +-1, applied exactly in the split pass).  lower: skip
+// the 128 x 128 tiles entirely above the diagonal (symmetric updates that only
+// need C's lower triangle).  err: device word set to 4 on a barrier time-out.
 int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const float* B,
-                          int ldb, float* C, int ldc, int* err, cudaStream_t stream) {
+                          int ldb, float* C, int ldc, int* err, cudaStream_t stream,
+                          float sa, int lower) {
     if (M <= 0 || N <= 0 || K <= 0) return RC_OK;
     if (((uintptr_t)A_T & 15) || ((uintptr_t)B & 15) || (lda & 3) || (ldb & 3)) {
         set_error("tcgen05 GEMM operands must be 16-byte aligned");
@@ -357,7 +364,8 @@ int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const 
         attr[dev] = true;
     }
     dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
-    feedback_gemm_tc_kernel<<<grid, 128, kGemmSmem, stream>>>(tmA, tmB, C, ldc, M, N, K, err);
+    feedback_gemm_tc_kernel<<<grid, 128, kGemmSmem, stream>>>(tmA, tmB, C, ldc, M, N, K, sa,
+                                                                lower, err);
     note_launch();
     return check_cuda(cudaGetLastError(), "feedback_gemm_tc launch") ? RC_DEVICE_ERROR : RC_OK;
 }

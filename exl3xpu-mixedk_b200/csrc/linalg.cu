@@ -201,19 +201,59 @@ __global__ void zero_upper_kernel(T* __restrict__ A, int n) {
     }
 }
 
+// PT[c][r] = P[r][c] for the rows x cols panel P (row pitch ldp); PT row pitch
+// ldt.  32 x 32 tiles through shared memory (coalesced both ways).
+__global__ void __launch_bounds__(256)
+transpose_panel_kernel(const float* __restrict__ P, int ldp, int rows, int cols,
+                       float* __restrict__ PT, int ldt) {
+    __shared__ float tile[32][33];
+    const int r0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
+    for (int k = ty; k < 32; k += 8) {
+        const int r = r0 + k, c = c0 + tx;
+        tile[k][tx] = (r < rows && c < cols) ? P[(size_t)r * ldp + c] : 0.0f;
+    }
+    __syncthreads();
+    for (int k = ty; k < 32; k += 8) {
+        const int c = c0 + k, r = r0 + tx;
+        if (c < cols && r < rows) PT[(size_t)c * ldt + r] = tile[tx][k];
+    }
+}
+
+size_t ldl_panel_bytes(int n) { return (size_t)kNB * n * sizeof(float); }
+
+// Blocked right-looking Cholesky (panel kNB): diagonal block, panel solve,
+// trailing update A[j0+nb:, j0+nb:] -= P . P^T (P = A[j0+nb:, j0:j0+nb]).
+// fp32 with panel_ws: the trailing update runs on tcgen05 tensor cores
+// (3xTF32, gemm_tc.cu) from a transposed copy of the panel, over the 128 x 128
+// tiles that reach the lower triangle -- the entries above the diagonal that
+// the diagonal tiles also write are never read and are zeroed at the end.  fp64 (and fp32 without panel_ws): SIMT update of
+// the lower triangle.
 template <typename T>
-int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream) {
+int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_ws,
+                   int* gemm_err) {
     for (int j0 = 0; j0 < n; j0 += kNB) {
         const int nb = (n - j0) < kNB ? (n - j0) : kNB;
         potrf_diag_kernel<T><<<1, 1024, 0, stream>>>(A, n, j0, nb, dstatus);
         const int rest = n - j0 - nb;
         if (rest > 0) {
             trsm_panel_kernel<T><<<(rest + 127) / 128, 128, 0, stream>>>(A, n, j0, nb, dstatus);
-            // A[j0+nb:, j0+nb:] -= P . P^T   (P = A[j0+nb:, j0:j0+nb])
             T* P = A + (size_t)(j0 + nb) * n + j0;
             T* C = A + (size_t)(j0 + nb) * n + (j0 + nb);
-            int rc = gemm_launch<T, true, true, true>(rest, rest, nb, P, n, P, n, C, n,
+            int rc;
+            if (sizeof(T) == 4 && panel_ws) {
+                const int ldt = (rest + 3) & ~3;
+                dim3 g((rest + 31) / 32, (nb + 31) / 32);
+                transpose_panel_kernel<<<g, 256, 0, stream>>>(
+                    reinterpret_cast<const float*>(P), n, rest, nb, panel_ws, ldt);
+                note_launch();
+                rc = launch_gemm_tn_acc_tc(rest, rest, nb, panel_ws, ldt, panel_ws, ldt,
+                                           reinterpret_cast<float*>(C), n, gemm_err, stream,
+                                           -1.0f, 1);
+            } else {
+                rc = gemm_launch<T, true, true, true>(rest, rest, nb, P, n, P, n, C, n,
                                                       T(-1), T(1), dstatus, stream);
+            }
             if (rc) return rc;
         }
         note_launch(rest > 0 ? 2 : 1);
@@ -296,8 +336,9 @@ dl_apply_kernel(const T* __restrict__ L, int n, const T* __restrict__ DLi,
 }
 
 template <typename T>
-int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream_t stream) {
-    int rc = cholesky_lower<T>(A, n, dstatus, stream);
+int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream_t stream,
+              float* panel_ws, int* gemm_err) {
+    int rc = cholesky_lower<T>(A, n, dstatus, stream, panel_ws, gemm_err);
     if (rc) return rc;
     dl_inverse_kernel<T><<<n / 16, 256, 0, stream>>>(A, n, dDLi, dD);
     dim3 g((n + 255) / 256, n / 16);
@@ -306,8 +347,10 @@ int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream
     return check_cuda(cudaGetLastError(), "block_ldl launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
-template int block_ldl<float>(float*, int, float*, float*, float*, int*, cudaStream_t);
-template int block_ldl<double>(double*, int, float*, double*, double*, int*, cudaStream_t);
+template int block_ldl<float>(float*, int, float*, float*, float*, int*, cudaStream_t, float*,
+                              int*);
+template int block_ldl<double>(double*, int, float*, double*, double*, int*, cudaStream_t,
+                               float*, int*);
 
 // ------------------------------------------------------------ quantize() U path
 // Ui = U^-1 for upper-triangular U (fp64), column by column (one thread per

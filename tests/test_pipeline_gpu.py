@@ -342,3 +342,20 @@ def test_lazy_sweep_dual_check(xq, oracle, mul1_lut, k, n, K, buf_cols, pivot, m
     assert bad.size == 0, f"{bad.size} tiles differ, first {bad[:5]}"
     lut = xq.get_lut("exl3_mul1").to(dev)
     assert torch.equal(xq.decode_trellis(trl[0], lut, K, k, n), hatW)
+
+
+def test_block_ldl_tensor_core_update(xq):
+    """fp32 block LDL (tensor-core trailing updates, many 128 x 128 tiles, the
+    lower-triangle tile skip) against the fp64 SIMT factorisation of the same
+    SPD matrix."""
+    gen = torch.Generator().manual_seed(70)
+    k = 2048
+    A = torch.randn(k, k, generator=gen, dtype=torch.float64)
+    G = A.t() @ A / k + 0.05 * torch.eye(k, dtype=torch.float64)
+    L32, D32 = xq.block_LDL(G.float(), 16)
+    L64, D64 = xq.block_LDL(G, 16)
+    assert torch.all(torch.triu(L32, 1) == 0)
+    rel = (L32.double() - L64.double()).abs().max() / L64.double().abs().max()
+    assert rel < 2e-4, rel
+    relD = (D32.double() - D64.double()).abs().max() / D64.double().abs().max()
+    assert relD < 2e-4, relD
