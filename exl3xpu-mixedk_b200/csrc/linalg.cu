@@ -117,36 +117,32 @@ __device__ __forceinline__ T dsqrt(T v);
 template <> __device__ __forceinline__ float dsqrt<float>(float v) { return sqrtf(v); }
 template <> __device__ __forceinline__ double dsqrt<double>(double v) { return sqrt(v); }
 
-// Factor the kNB x kNB diagonal block at (j0, j0) in place (lower).
+// Factor the kNB x kNB diagonal block at (j0, j0) in place (lower).  1024
+// threads as 32 x 32; every thread derives the pivot's square root from
+// shared memory itself (the same value everywhere), so a column costs two
+// barriers: scale the column, then the rank-1 update of the trailing lower
+// triangle, 2-D strided without integer division.
 template <typename T>
 __global__ void __launch_bounds__(1024)
 potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ status) {
     __shared__ T S[kNB][kNB + 1];
-    __shared__ int bad;
     if (*status) return;
     const int t = threadIdx.x;
-    for (int idx = t; idx < nb * nb; idx += blockDim.x) {
-        const int r = idx / nb, c = idx % nb;
-        S[r][c] = A[(size_t)(j0 + r) * n + (j0 + c)];
-    }
-    if (t == 0) bad = 0;
+    const int tx = t & 31, ty = t >> 5;
+    for (int r = ty; r < nb; r += 32)
+        for (int c = tx; c < nb; c += 32) S[r][c] = A[(size_t)(j0 + r) * n + (j0 + c)];
     __syncthreads();
+    int bad = 0;
     for (int j = 0; j < nb; ++j) {
-        if (t == 0) {
-            const T d = S[j][j];
-            if (!(d > T(0)) || !isfinite((double)d)) bad = j0 + j + 1;
-            else S[j][j] = dsqrt<T>(d);
-        }
+        const T d = S[j][j];
+        if (!(d > T(0)) || !isfinite((double)d)) { bad = j0 + j + 1; break; }
+        const T djj = dsqrt<T>(d);
+        if (t < nb - j - 1) S[j + 1 + t][j] = S[j + 1 + t][j] / djj;
         __syncthreads();
-        if (bad) break;
-        const T djj = S[j][j];
-        for (int i = j + 1 + t; i < nb; i += blockDim.x) S[i][j] = S[i][j] / djj;
-        __syncthreads();
-        // trailing rank-1 update of the lower triangle
-        const int m = nb - j - 1;
-        for (int idx = t; idx < m * m; idx += blockDim.x) {
-            const int i = j + 1 + idx / m, c = j + 1 + idx % m;
-            if (c <= i) S[i][c] = S[i][c] - S[i][j] * S[c][j];
+        if (t == 0) S[j][j] = djj;
+        for (int i = j + 1 + ty; i < nb; i += 32) {
+            const T lij = S[i][j];
+            for (int c = j + 1 + tx; c <= i; c += 32) S[i][c] = S[i][c] - lij * S[c][j];
         }
         __syncthreads();
     }
@@ -154,10 +150,8 @@ potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ st
         if (t == 0) *status = bad;
         return;
     }
-    for (int idx = t; idx < nb * nb; idx += blockDim.x) {
-        const int r = idx / nb, c = idx % nb;
-        if (c <= r) A[(size_t)(j0 + r) * n + (j0 + c)] = S[r][c];
-    }
+    for (int r = ty; r < nb; r += 32)
+        for (int c = tx; c <= r; c += 32) A[(size_t)(j0 + r) * n + (j0 + c)] = S[r][c];
 }
 
 // Rows i >= j0+nb: A[i, j0:j0+nb] <- A[i, j0:j0+nb] . L_jj^-T (forward
