@@ -82,6 +82,22 @@ def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+def _out(t: torch.Tensor, od: torch.device) -> torch.Tensor:
+    """Result tensor on the output device.  Device -> host copies go into pinned
+    memory asynchronously on the current stream; the caller synchronises once
+    (_out_done) before handing the results out."""
+    if od.type == "cpu" and t.is_cuda:
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t, non_blocking=True)
+        return h
+    return t.to(od)
+
+
+def _out_done(dev: torch.device, od: torch.device):
+    if od.type == "cpu":
+        torch.cuda.current_stream(dev).synchronize()
+
+
 def _select(dev: torch.device):
     call("exl3b_device_init", dev.index)
 
@@ -527,6 +543,7 @@ def quantize_linear_fused(Ws: list, H_x: torch.Tensor | None, code: str = "exl3_
     del Wq, Lfac
 
     od = torch.device(out_device) if out_device is not None else dev
+    wscales = torch.cat([m["Wscale_d"] for m in members]).tolist()   # one host sync
     outs = []
     c0 = 0
     for j, mem in enumerate(members):
@@ -545,19 +562,20 @@ def quantize_linear_fused(Ws: list, H_x: torch.Tensor | None, code: str = "exl3_
                  mem["Wscale_d"].data_ptr(), su32.data_ptr(), sv32.data_ptr(),
                  W_hat.data_ptr(), _stream(dev))
         out = {
-            "W_hat": W_hat.to(od),
-            "trellis": trl[j].to(od),
-            "suh": suh_j.to(od), "svh": svh_j.to(od),
-            "Wscale": float(mem["Wscale_d"].item()), "lut_rms": float(lut_rms),
+            "W_hat": _out(W_hat, od),
+            "trellis": _out(trl[j], od),
+            "suh": _out(suh_j, od), "svh": _out(svh_j, od),
+            "Wscale": float(wscales[j]), "lut_rms": float(lut_rms),
             "code": code, "K": int(Ks[j]), "L": L, "V": 1, "use_ldlq": use_ldlq,
             "channel_scales": channel_scales,
         }
         if keep_states:
-            out["states"] = (st if len(members) == 1 else
-                             st[:, c0 // 16:(c0 + m_out) // 16].contiguous()).to(od)
-            out["hatWq"] = hw.to(od)
+            out["states"] = _out(st if len(members) == 1 else
+                             st[:, c0 // 16:(c0 + m_out) // 16].contiguous(), od)
+            out["hatWq"] = _out(hw, od)
         outs.append(out)
         c0 += m_out
+    _out_done(dev, od)
     return outs
 
 
@@ -628,7 +646,10 @@ def quantize(W_transformed: torch.Tensor, U_upper: torch.Tensor | None,
     call("exl3b_transpose_scale", 1, hatW.data_ptr(), k_in, m_out, _ptr(sv_m), _ptr(su_m),
          scale.data_ptr(), W_hat.data_ptr(), None, s)
     od = W_transformed.device
-    return W_hat.to(od), trl[0].to(od), float(scale.item())
+    sc = float(scale.item())
+    W_hat, tr = _out(W_hat, od), _out(trl[0], od)
+    _out_done(dev, od)
+    return W_hat, tr, sc
 
 
 def prepare_incoherence(W, H_x=None, su_seed=20261011, sv_seed=None, su_sign=None,

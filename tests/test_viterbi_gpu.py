@@ -136,3 +136,19 @@ def test_serve_worker_matches_oracle(oracle, mul1_lut):
     finally:
         del os.environ["XTQ_VIT_MAXSEQ"]
     assert np.array_equal(st.t().numpy(), ref.astype(np.int64))
+
+
+def test_xtq_vit_run_lazy_batch(oracle, mul1_lut):
+    """xtq_vit_run with >= 2 sequences per SM runs the lazy-argmin pipeline
+    behind the reference's ctypes signature: same states as the oracle."""
+    from exl3b import native
+    L = native.lib()
+    rng = np.random.default_rng(303)
+    X = rng.standard_normal((300, 256)).astype(np.float32)
+    X[:50] = np.round(X[:50] * 4) / 4                  # tie-heavy
+    out = np.zeros((300, 256), np.int32)
+    P = ctypes.c_void_p
+    rc = L.xtq_vit_run(X.ctypes.data_as(P), 300, b"mul1p", 0, 128, out.ctypes.data_as(P))
+    assert rc == 0, native.last_error()
+    ref = oracle.tailbite(X, mul1_lut, 4, pivot=128, margin=0, nthreads=NTHREADS)
+    assert np.array_equal(out, ref)
