@@ -273,7 +273,8 @@ int exl3b_u_to_gram(const float* dU, int k, double* dG, void* ws, size_t ws_byte
 // ------------------------------------------------------------------ LDLQ
 // Workspace: E [k][n] | prod [k][n] (LDLQ only) | backpointer slots |
 // control words (slot flags, per-column progress, ticket, error word) |
-// lazy-pipeline row regions (SMs x 2 x Lazy<K>::REGION, largest for K = 4).
+// lazy-pipeline row regions (SMs x 2 x Lazy<K>::REGION, largest for the
+// smallest K of the sweep).
 static int sweep_slots() { return device_sms() * ldlq_tile_max_resident_per_sm() + 16; }
 
 static size_t sweep_slot(const int* seg_K, int nseg) {
@@ -290,7 +291,7 @@ static size_t sweep_ctrl_bytes(int tn) {
 }
 
 static size_t sweep_lazy_bytes(int kmin) {
-    return align256((size_t)device_sms() * 2 * lazy_region_bytes(kmin > 4 ? kmin : 4));
+    return align256((size_t)device_sms() * 2 * lazy_region_bytes(kmin));
 }
 
 size_t exl3b_ldlq_workspace_bytes(int k, int n, int kmin, int use_ldlq) {

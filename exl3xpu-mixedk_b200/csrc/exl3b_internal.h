@@ -51,9 +51,14 @@ int build_f2tab(int K, const __half* lut16, uint4* tab, cudaStream_t stream);
 
 // Tail-biting encode of nseq sequences X [nseq][256] -> states [nseq][256].
 // Standalone encoder plan for (nseq, K) on a device with `sms` SMs: the
-// lazy-argmin pipeline (K >= 4, at least two sequences per SM; grid = SMs,
-// two row regions per CTA) or the traced encoder (grid = min(nseq, SMs),
-// one backpointer slot per CTA); bytes = workspace needed.
+// lazy-argmin pipeline (K >= kLazyMinK, at least two sequences per SM; grid =
+// SMs, two row regions per CTA) or the traced encoder (grid = min(nseq, SMs),
+// one backpointer slot per CTA); bytes = workspace needed.  The same rule
+// picks the LDLQ sweep's tile kernel per launch.
+constexpr int kLazyMinK = 2;
+inline bool lazy_pipeline(int K, long long units, int sms) {
+    return K >= kLazyMinK && sms > 0 && units >= 2LL * sms;
+}
 struct TailbitePlan { bool lazy; int grid; size_t bytes; };
 TailbitePlan tailbite_plan(int nseq, int K, int sms);
 size_t lazy_region_bytes(int K);
@@ -135,7 +140,7 @@ struct SweepArgs {
     float* xout;
     uint8_t* bp_ws;
     size_t bp_slot;
-    float* lazy_ws;          // lazy pipeline: SMs x 2 row regions (K >= 4 launches)
+    float* lazy_ws;          // lazy pipeline: SMs x 2 row regions (lazy_pipeline launches)
     int nslots;              // backpointer slots (> SM count)
     int* slots;              // [nslots] ownership flags (zero at sweep start)
     int* colprog;            // [tn] finished k-blocks per column (zero at start)

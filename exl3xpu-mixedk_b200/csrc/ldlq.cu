@@ -11,8 +11,8 @@
 //
 // Sweep (host loop, all launches on one stream): k-blocks right to left in
 // 128-row buffers.  One tile-kernel launch per buffer covers all its k-blocks x
-// column tiles.  K >= 4 launches with at least two tiles per SM use the
-// persistent lazy-argmin kernel (ldlq_lazy.cu); the others, one CTA per tile
+// column tiles.  Launches with at least two tiles per SM use the persistent
+// lazy-argmin kernel (ldlq_lazy.cu); the others, one CTA per tile
 // with the traced encoder, below.  Each CTA takes a ticket in dependency order (k-block
 // descending, column ascending) and, when it needs the block below it in the
 // same column (intra-buffer feedback), waits on that column's progress
@@ -242,8 +242,8 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
             const long long nb = (long long)(hi - lo) * p.ls_pre[p.nls];
             p.ntiles = (int)nb;
             prof_begin_launch(stream, PROF_TILE, (double)nb * 256.0);
-            // K >= 4 with at least two tiles per SM: persistent CTAs, lazy argmin
-            const bool lazy = K >= 4 && a.lazy_ws != nullptr && sms > 0 && nb >= 2LL * sms;
+            // at least two tiles per SM: persistent CTAs, lazy argmin
+            const bool lazy = a.lazy_ws != nullptr && lazy_pipeline(K, nb, sms);
             const int rc = lazy ? launch_lazy_tile(K, p, (unsigned)sms, stream)
                                 : launch_tile(K, p, (unsigned)nb, stream);
             prof_end_launch(stream);

@@ -1,5 +1,5 @@
 // ldlq_lazy.cu -- the LDLQ sweep's tile kernel with the lazy-argmin encoder
-// (vit_lazy.cuh), used for K >= 4 launches with at least two tiles per SM.
+// (vit_lazy.cuh), used for launches with at least two tiles per SM.
 //
 // Persistent CTAs (one per SM, 16 forward warps + the traceback warp) take
 // tiles by ticket in the same dependency order as the one-tile-per-CTA kernel
@@ -263,12 +263,14 @@ static int launch_lazy_tile_k(const LdlqTileParams& p, unsigned grid, cudaStream
 
 int launch_lazy_tile(int K, const LdlqTileParams& p, unsigned grid, cudaStream_t stream) {
     switch (K) {
+        case 2: return launch_lazy_tile_k<2>(p, grid, stream);
+        case 3: return launch_lazy_tile_k<3>(p, grid, stream);
         case 4: return launch_lazy_tile_k<4>(p, grid, stream);
         case 5: return launch_lazy_tile_k<5>(p, grid, stream);
         case 6: return launch_lazy_tile_k<6>(p, grid, stream);
         case 7: return launch_lazy_tile_k<7>(p, grid, stream);
     }
-    set_error("lazy tile kernel: K=%d outside 4..7", K);
+    set_error("lazy tile kernel: K=%d outside 2..7", K);
     return RC_BAD_K;
 }
 

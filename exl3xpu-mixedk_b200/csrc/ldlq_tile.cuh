@@ -149,7 +149,7 @@ __device__ __forceinline__ void tile_writeback(const LdlqTileParams& p, int i, i
     }
 }
 
-// ldlq_lazy.cu: persistent lazy-argmin tile kernel for K = 4..7, `grid` CTAs
+// ldlq_lazy.cu: persistent lazy-argmin tile kernel for K = 2..7, `grid` CTAs
 int launch_lazy_tile(int K, const LdlqTileParams& p, unsigned grid, cudaStream_t stream);
 
 }  // namespace exl3b

@@ -1,16 +1,20 @@
-// vit_lazy.cuh -- tail-biting Viterbi with the argmin taken lazily (K >= 4).
+// vit_lazy.cuh -- tail-biting Viterbi with the argmin taken lazily.
 //
 // Same trellis, costs and results as vit_tailbite (viterbi.cuh), bit for bit:
 // only where each step's predecessor choice is decided changes.
 //
 //  * Forward passes keep the minimum only (the "untraced" ACS: two
 //    subtractions, one packed square, one packed add, one three-input min per
-//    predecessor pair -- about half the work of tracking the argmin), and each
-//    thread streams its outputs best_{i+1}[j] of every step the traceback will
-//    cross to a per-tile row region in global memory (natural index order,
-//    row q = best_q).  The end state of a pass (the first-index argmin over
-//    the last step's costs) is found by rescanning only the group(s) that
-//    reach the minimum.
+//    predecessor pair -- about half the work of tracking the argmin).  Every
+//    step the traceback will cross leaves its output array best_{i+1} in
+//    shared memory; one thread copies that array, as it lies there (the
+//    Geo<K>::baddr layout), to the tile's row region in global memory with a
+//    TMA bulk store (row q = best_q).  The forward threads themselves issue no
+//    global stores, so the per-step barrier never waits for global writes to
+//    be acknowledged; the copy engine reads the buffer while the next step
+//    runs.  The end state of a pass (the first-index argmin over the last
+//    step's costs) is found by rescanning only the group(s) that reach the
+//    minimum.
 //  * The traceback recomputes, for the one group j = s >> K on the path, the
 //    2^K candidate costs cost_{r-1}(j + w 2^(16-K)) = fl(fl(f - x)^2) + best_{r-1}
 //    from the stored row with the same fp32 operations as the forward step,
@@ -31,8 +35,9 @@
 //        F2(A) | T1(B)
 //        F2(B) | T2(A)
 //    A phase ends when both its forward pass and its traceback are done.
-//  * K = 2, 3 keep the tracked encoder: their rows (64 / 32 KB per step) would
-//    cost more HBM traffic than the argmin tracking they save.
+//  * Rows are 2^(18-K) bytes per step (K = 2: 64 KB, K = 4: 16 KB, K = 7:
+//    2 KB).  At K = 2 the row writes approach HBM bandwidth and bound the
+//    forward pass; every K still runs faster than with the tracked encoder.
 #pragma once
 #include "viterbi.cuh"
 
@@ -44,9 +49,34 @@ template <int K>
 struct Lazy {
     using G = Geo<K>;
     static constexpr int ROWS = kSteps - 1;                       // rows 1..254 used
-    static constexpr size_t REGION = (size_t)ROWS * G::SPRE * 4;  // bytes per tile region
+    static constexpr int ROW_BYTES = G::SPRE * 4;                 // one best array
+    static constexpr size_t REGION = (size_t)ROWS * ROW_BYTES;    // bytes per tile region
     static constexpr int NPL = G::NC > 32 ? G::NC / 32 : 1;       // candidates per lane
+    // a row is the shared-memory image of one best array, unpadded
+    static_assert(VitSmem<K>::B_BYTES == ROW_BYTES, "row = smem best array");
+    static_assert(ROW_BYTES % 16 == 0, "bulk copies move multiples of 16 bytes");
 };
+
+// TMA bulk store of one best array (shared -> global, async proxy), its
+// bulk-group bookkeeping, and the proxy fences around it.
+__device__ __forceinline__ void row_fence_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void row_copy(float* dst, const float* src, int bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n\t"
+                 "cp.async.bulk.commit_group;"
+                 :: "l"(dst), "r"((uint32_t)__cvta_generic_to_shared(src)), "r"(bytes)
+                 : "memory");
+}
+// every issued copy has read its shared-memory source
+__device__ __forceinline__ void row_copies_read() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// every issued copy is complete in global memory and ordered before this
+// thread's later generic-proxy accesses
+__device__ __forceinline__ void row_copies_done() {
+    asm volatile("cp.async.bulk.wait_group 0;\n\tfence.proxy.async.global;" ::: "memory");
+}
 
 // Traceback job state (shared memory; read by all lanes of the job warp,
 // written by its lane 0).  r: the next row to resolve (s = s_r known); rows r-1 .. stop are
@@ -83,8 +113,9 @@ struct LazySmem {
 
 // Run the armed traceback job to its end (the job warp; every lane calls it;
 // job state in registers).  Per row r (s = s_r known; group j = s >> K): lane
-// w (and w + 32, ... for K >= 6) loads best_{r-1}[(j >> K) + w P] (L2-coherent:
-// the rows were written by other warps) and the decode value of predecessor
+// w (and w + 32, ... for K >= 6) loads best_{r-1}[(j >> K) + w P] at its
+// Geo<K>::baddr position in the row (L2-coherent: the rows were written by
+// the copy engine; for K >= 6 the 2^K values are contiguous) and the decode value of predecessor
 // j + w 2^(16-K), forms the forward step's cost fl(fl(f - x)^2) + best, and
 // the warp takes the lexicographic (cost, w) minimum with two redux.sync
 // minima (costs are >= +0 or +inf, so their bit patterns order like the
@@ -122,7 +153,7 @@ __device__ __forceinline__ void tb_job_run(char* smem, const float* __restrict__
             if (w < G::NC) {
                 const int idx = m + w * G::P;
                 const float b = (q == 0) ? ((overlap < 0 || idx == overlap) ? 0.0f : INF)
-                                         : __ldcg(row + idx);
+                                         : __ldcg(row + G::baddr(idx));
                 const float d = __fsub_rn(__ldg(lut32 + j + (w << (16 - K))), x);
                 const uint32_t c = __float_as_uint(__fadd_rn(__fmul_rn(d, d), b));
                 if (c < kc) { kc = c; kw = (uint32_t)w; }
@@ -203,16 +234,22 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
     asm volatile("ld.volatile.shared.f32 %0, [%1];" : "=f"(zr)
                  : "r"((uint32_t)__cvta_generic_to_shared(zword)));
 
-    // rows the traceback reads: best_q, q in [max(stop, 1), nsteps - 2]
+    // rows the traceback reads: best_q, q in [max(stop, 1), nsteps - 2].
+    // Step i writes best_{i+1} into Bn; after the step barrier thread 0 copies
+    // it to row i + 1.  Step i + 2 overwrites that buffer, so before the
+    // barrier that ends step i + 1 thread 0 waits until the copy has read it.
     const int lo = max(stop, 1), hi = nsteps - 2;
     if (t < kVT) {
         for (int i = 0; i < nsteps - 1; ++i) {
             const float x = xs[(i - rol) & 255];
-            float* grow = (i + 1 >= lo && i + 1 <= hi) ? rows + (size_t)(i + 1) * G::SPRE
-                                                       : nullptr;
-            vit_step<K, false>(f2, x, Bc, Bn, t, zr, grow);
+            vit_step<K, false>(f2, x, Bc, Bn, t, zr);
             float* tmp = Bc; Bc = Bn; Bn = tmp;
+            const bool keep = i + 1 >= lo && i + 1 <= hi;
+            if (keep) row_fence_shared();       // this thread's writes -> async proxy
+            if (t == 0) row_copies_read();      // the previous row's source is free
             asm volatile("bar.sync 1, %0;" :: "r"(kVT) : "memory");
+            if (keep && t == 0)
+                row_copy(rows + (size_t)(i + 1) * G::SPRE, Bc, Lazy<K>::ROW_BYTES);
         }
         // final step, untraced: best_n[j] = min_w cost_{n-1}(j + w 2^(16-K)).
         // The pass ends at the first-index argmin over cost_{n-1}: the lowest
@@ -256,6 +293,9 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
         for (int off = 16; off > 0; off >>= 1)
             bs = min(bs, __shfl_xor_sync(0xffffffffu, bs, off));
         if ((t & 31) == 0) reds[t >> 5] = bs;
+        // the rows are in global memory before the pass ends (the next phase's
+        // traceback reads them)
+        if (t == 0) row_copies_done();
     } else {
         tb_job_run<K>(smem, lut32, t - kVT);
     }

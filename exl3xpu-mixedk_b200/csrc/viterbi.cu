@@ -14,7 +14,7 @@
 
 namespace exl3b {
 
-// Batches of at least two sequences per SM at K >= 4 go through the lazy-argmin
+// Batches of at least two sequences per SM go through the lazy-argmin
 // pipeline instead (vit_lazy.cuh): SM-count persistent CTAs, CTA b encoding
 // sequences b, b + grid, b + 2 grid, ... two at a time, with two row regions of
 // the workspace (Lazy<K>::REGION bytes each).  Its loop state lives in shared
@@ -227,6 +227,8 @@ static int launch_lazy_k(const float* dX, int nseq, int pivot, int margin, int32
 
 size_t lazy_region_bytes(int K) {
     switch (K) {
+        case 2: return Lazy<2>::REGION;
+        case 3: return Lazy<3>::REGION;
         case 4: return Lazy<4>::REGION;
         case 5: return Lazy<5>::REGION;
         case 6: return Lazy<6>::REGION;
@@ -237,7 +239,7 @@ size_t lazy_region_bytes(int K) {
 
 TailbitePlan tailbite_plan(int nseq, int K, int sms) {
     TailbitePlan p;
-    p.lazy = K >= 4 && sms > 0 && nseq >= 2 * sms;
+    p.lazy = lazy_pipeline(K, nseq, sms);
     p.grid = p.lazy ? sms : (nseq < sms ? nseq : sms);
     p.bytes = p.lazy ? (size_t)p.grid * 2 * lazy_region_bytes(K)
                      : (size_t)p.grid * bp_slot_bytes(K);
@@ -250,6 +252,8 @@ int launch_tailbite(const float* dX, int nseq, int K, int pivot, int margin,
     const int grid = plan.grid;
     if (plan.lazy) {
         switch (K) {
+            case 2: return launch_lazy_k<2>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
+            case 3: return launch_lazy_k<3>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
             case 4: return launch_lazy_k<4>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
             case 5: return launch_lazy_k<5>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);
             case 6: return launch_lazy_k<6>(dX, nseq, pivot, margin, dStates, ws, grid, f2tab, lut32, stream);

@@ -319,12 +319,14 @@ def test_stored_fields_dequantise_to_w_hat(xq, tmp_path):
     (256, 768, 4, 128, 128, 0),      # 8 x 48 = 384 tiles per buffer launch
     (256, 640, 5, 128, 7, 16),       # short first pass
     (256, 1184, 7, 128, 200, 100),
+    (256, 768, 3, 128, 128, 0),      # whole-butterfly geometries (K = 2, 3)
+    (256, 640, 2, 128, 7, 16),
     (2560, 160, 6, 1024, 128, 0),    # 10 columns, 64-block buffers: a CTA's own
                                      # pending tiles are often a new tile's dependency
     (4864, 16, 4, 4864, 128, 0),     # one column: every B depends on its A
 ])
 def test_lazy_sweep_dual_check(xq, oracle, mul1_lut, k, n, K, buf_cols, pivot, margin):
-    """Buffer launches of >= 2 tiles per SM at K >= 4 run the persistent
+    """Buffer launches of >= 2 tiles per SM run the persistent
     lazy-argmin tile kernel: every k-block's encoder targets, re-encoded by the
     CPU oracle, give the sweep's states (the reference's per-launch dual
     check), and the trellis decodes to hatW."""

@@ -49,9 +49,10 @@ def test_golden_states(ops, K):
     (4, 160, 0, 16),       # quantize() defaults at seed 0 (traced encoder)
     (2, 48, 77, 16), (3, 48, 255, 0), (5, 48, 3, 40),
     (6, 48, 128, 0), (7, 48, 200, 100),
-    # lazy pipeline at every K >= 4 with short / full / pivot-0 first passes
+    # lazy pipeline at every K with short / full / pivot-0 first passes
     (4, 444, 0, 16), (5, 301, 3, 40), (6, 297, 255, 0), (7, 445, 200, 100),
     (5, 296, 128, 0), (7, 310, 0, 0),
+    (2, 300, 77, 16), (2, 297, 0, 0), (3, 298, 255, 0), (3, 333, 128, 0),
 ])
 def test_random_vs_oracle(ops, oracle, mul1_lut, K, nseq, pivot, margin):
     rng = np.random.default_rng(1000 + K * 7 + pivot)
