@@ -52,7 +52,15 @@ METRIC = "trellis-encoded weights/s (Viterbi+LDLQ) at K=4"
 UNIT = "weights/s"
 K_BITS = 4
 DIM = 5120
-OPS_PER_WEIGHT = 2 * 2 * 65536      # 2 passes x 2^16 ACS x 2 ops (margin 0)
+# Per weight (one trellis step per weight and pass, 2 passes at margin 0):
+# 2 x 2^16 add-compare-selects, each 3 correctly rounded fp32 operations
+# (f - x, its square, + best: fusing any two would change the rounding); the
+# minimum runs on the ALU pipe beside them.  The fp32 pipe retires 128 lane
+# operations per SM per clock (the packed f32x2 forms issue at half rate, so
+# they save issue slots but not fp32 throughput).
+OPS_PER_WEIGHT = 2 * 65536 * 3
+FP32_NOTE = ("3 rounded fp32 ops (sub, square, add) per add-compare-select; "
+             "the min runs on the ALU pipe")
 WORKLOAD = ("config 2: single dense projection 5120x5120 bf16 ~N(0,0.02^2) + 0.1% x10 "
             "outliers; H = A^T A/4096, A Student-t(4) x lognormal(1) channel scales; "
             "random-sign Hadamard, damped block-LDL, full BlockLDLQ + tail-biting "
@@ -263,9 +271,9 @@ def _kernels(L, steps, step_ms, sms, peaks):
     src = "MEASURED_PEAKS.json" if peaks else "fallback"
     out = {}
     specs = [
-        (0, "ldlq_tile", "alu", "Gop/s", lambda u: u * OPS_PER_WEIGHT / 1e9,
+        (0, "ldlq_tile", "fp32", "Gop/s", lambda u: u * OPS_PER_WEIGHT / 1e9,
          sms * 128 * mhz * 1e6 / 1e9,
-         f"{sms} SMs x 128 lanes x {mhz:.0f} MHz; 2 ops per add-compare-select"),
+         f"{sms} SMs x 128 fp32 lanes x {mhz:.0f} MHz; {FP32_NOTE}"),
         (1, "feedback_gemm_tcgen05", "tensor", "TFLOP/s", lambda u: u / 1e12, bf16 / 2.0,
          f"TF32 dense = bf16 dense / 2 of {src} (useful FLOP; 3xTF32 issues 3 MMAs per "
          "useful product, so frac <= 1/3)"),
@@ -420,11 +428,11 @@ def main():
     tpw = _profile_traffic()
     roofline = {
         "kernel": "LDLQ tile kernel (fused feedback + tail-biting Viterbi + write-back; "
-                  "ldlq_lazy_kernel for K>=4 launches of >= 2 tiles per SM)",
-        "bound": "alu", "achieved": achieved, "peak": peak_ops, "unit": "Gop/s",
+                  "ldlq_lazy_kernel for launches of >= 2 tiles per SM)",
+        "bound": "fp32", "achieved": achieved, "peak": peak_ops, "unit": "Gop/s",
         "frac": achieved / peak_ops,
-        "peak_source": f"{sms} SMs x 128 lanes x {mhz:.0f} MHz (sm_max_mhz of "
-                       "MEASURED_PEAKS.json); 2 ops per add-compare-select",
+        "peak_source": f"{sms} SMs x 128 fp32 lanes x {mhz:.0f} MHz (sm_max_mhz of "
+                       f"MEASURED_PEAKS.json); {FP32_NOTE}",
         "ops_per_weight": OPS_PER_WEIGHT,
         "launches_per_step": n_tile / args.steps,
         "avg_launch_ms": tile_ms_avg,

@@ -6,13 +6,18 @@
 //  * Forward passes keep the minimum only (the "untraced" ACS: two
 //    subtractions, one packed square, one packed add, one three-input min per
 //    predecessor pair -- about half the work of tracking the argmin).  Every
-//    step the traceback will cross leaves its output array best_{i+1} in
-//    shared memory; one thread copies that array, as it lies there (the
-//    Geo<K>::baddr layout), to the tile's row region in global memory with a
-//    TMA bulk store (row q = best_q).  The forward threads themselves issue no
-//    global stores, so the per-step barrier never waits for global writes to
-//    be acknowledged; the copy engine reads the buffer while the next step
-//    runs.  The end state of a pass (the first-index argmin over the last
+//    step the traceback will cross is kept as a row of the tile's row region
+//    in global memory (row q = best_q), in one of two ways (Lazy<K>::BULK):
+//    - K <= 4 (rows of 16 to 64 KB): the best arrays rotate through a ring
+//      in shared memory (Lazy<K>::RING arrays), and each time half a ring of
+//      rows is complete one thread copies them, as they lie there (the
+//      Geo<K>::baddr layout), with one TMA bulk store.  The forward threads
+//      issue no global stores, so the per-step barrier never waits for
+//      global writes to be acknowledged, and the proxy fence that hands their
+//      shared-memory writes to the copy engine is paid once per batch.
+//    - K >= 5 (rows of 8 KB and less): each thread stores its outputs of the
+//      step to the row itself (natural index order, one or two vector
+//      stores), which measured faster there than the copy engine.  The end state of a pass (the first-index argmin over the last
 //    step's costs) is found by rescanning only the group(s) that reach the
 //    minimum.
 //  * The traceback recomputes, for the one group j = s >> K on the path, the
@@ -45,6 +50,10 @@ namespace exl3b {
 
 constexpr int kLazyThreads = kVT + 32;   // 16 forward warps + the job warp
 
+#ifndef EXL3B_LAZY_RING_KB
+#define EXL3B_LAZY_RING_KB 64    // shared memory of the best-array ring
+#endif
+
 template <int K>
 struct Lazy {
     using G = Geo<K>;
@@ -52,9 +61,18 @@ struct Lazy {
     static constexpr int ROW_BYTES = G::SPRE * 4;                 // one best array
     static constexpr size_t REGION = (size_t)ROWS * ROW_BYTES;    // bytes per tile region
     static constexpr int NPL = G::NC > 32 ? G::NC / 32 : 1;       // candidates per lane
+    // rows by TMA bulk store from a shared-memory ring (else by the threads)
+    static constexpr bool BULK = K <= 4;
+    // the ring of best arrays (64 KB: K = 2: 2, K = 3: 2, K = 4: 4; two when
+    // the threads store the rows) and the rows per bulk copy (half the ring,
+    // aligned: a batch's arrays are adjacent)
+    static constexpr int RING_FIT = (EXL3B_LAZY_RING_KB * 1024) / ROW_BYTES;
+    static constexpr int RING = (BULK && RING_FIT > 2) ? RING_FIT : 2;
+    static constexpr int BATCH = RING / 2;
     // a row is the shared-memory image of one best array, unpadded
     static_assert(VitSmem<K>::B_BYTES == ROW_BYTES, "row = smem best array");
     static_assert(ROW_BYTES % 16 == 0, "bulk copies move multiples of 16 bytes");
+    static_assert(RING >= 2 && (RING & (RING - 1)) == 0, "ring of 2^n arrays");
 };
 
 // TMA bulk store of one best array (shared -> global, async proxy), its
@@ -101,9 +119,8 @@ template <int K>
 struct LazySmem {
     using G = Geo<K>;
     static constexpr int B_BYTES = VitSmem<K>::B_BYTES;
-    static constexpr int OFF_B0 = 0;
-    static constexpr int OFF_B1 = B_BYTES;
-    static constexpr int OFF_X = 2 * B_BYTES;             // xs[2][256] fp32
+    static constexpr int OFF_RING = 0;                    // Lazy<K>::RING best arrays
+    static constexpr int OFF_X = Lazy<K>::RING * B_BYTES; // xs[2][256] fp32
     static constexpr int OFF_ST = OFF_X + 2048;           // st[2][256] int32
     static constexpr int OFF_RED = OFF_ST + 2048;         // reductions, broadcast words
     static constexpr int OFF_JOB = OFF_RED + 256;         // TbJob
@@ -114,8 +131,9 @@ struct LazySmem {
 // Run the armed traceback job to its end (the job warp; every lane calls it;
 // job state in registers).  Per row r (s = s_r known; group j = s >> K): lane
 // w (and w + 32, ... for K >= 6) loads best_{r-1}[(j >> K) + w P] at its
-// Geo<K>::baddr position in the row (L2-coherent: the rows were written by
-// the copy engine; for K >= 6 the 2^K values are contiguous) and the decode value of predecessor
+// position in the row (Geo<K>::baddr for bulk-copied rows, natural otherwise;
+// L2-coherent loads: other warps or the copy engine wrote the rows) and the
+// decode value of predecessor
 // j + w 2^(16-K), forms the forward step's cost fl(fl(f - x)^2) + best, and
 // the warp takes the lexicographic (cost, w) minimum with two redux.sync
 // minima (costs are >= +0 or +inf, so their bit patterns order like the
@@ -153,7 +171,7 @@ __device__ __forceinline__ void tb_job_run(char* smem, const float* __restrict__
             if (w < G::NC) {
                 const int idx = m + w * G::P;
                 const float b = (q == 0) ? ((overlap < 0 || idx == overlap) ? 0.0f : INF)
-                                         : __ldcg(row + G::baddr(idx));
+                                         : __ldcg(row + (Lazy<K>::BULK ? G::baddr(idx) : idx));
                 const float d = __fsub_rn(__ldg(lut32 + j + (w << (16 - K))), x);
                 const uint32_t c = __float_as_uint(__fadd_rn(__fmul_rn(d, d), b));
                 if (c < kc) { kc = c; kw = (uint32_t)w; }
@@ -217,8 +235,11 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
                                          const float* __restrict__ lut32, int t) {
     using G = Geo<K>;
     using SM = LazySmem<K>;
-    float* Bc = reinterpret_cast<float*>(smem + SM::OFF_B0);
-    float* Bn = reinterpret_cast<float*>(smem + SM::OFF_B1);
+    using L = Lazy<K>;
+    constexpr int BB = SM::B_BYTES / 4;                   // floats per best array
+    float* ring = reinterpret_cast<float*>(smem + SM::OFF_RING);
+    float* Bc = ring;                                     // best_i: ring slot i % RING
+    float* Bn = ring;
     const float* xs = reinterpret_cast<const float*>(smem + SM::OFF_X) + 256 * slot;
     float* redc = reinterpret_cast<float*>(smem + SM::OFF_RED);
     int* reds = reinterpret_cast<int*>(smem + SM::OFF_RED + 64);
@@ -235,22 +256,54 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
                  : "r"((uint32_t)__cvta_generic_to_shared(zword)));
 
     // rows the traceback reads: best_q, q in [max(stop, 1), nsteps - 2].
-    // Step i writes best_{i+1} into Bn; after the step barrier thread 0 copies
-    // it to row i + 1.  Step i + 2 overwrites that buffer, so before the
-    // barrier that ends step i + 1 thread 0 waits until the copy has read it.
+    // Step i writes best_{i+1} into ring slot (i + 1) % RING.  Rows go out in
+    // aligned batches of BATCH (rows b BATCH .. b BATCH + BATCH - 1, clipped to
+    // [lo, hi]; adjacent slots): when step i completes a batch, every thread
+    // fences its writes to the async proxy before the step barrier and thread
+    // 0 issues one bulk copy after it.  Before every step barrier thread 0
+    // waits until the copies issued so far have read their slots; the
+    // earliest reuse of a batch's slot is RING - BATCH >= 1 steps after that.
     const int lo = max(stop, 1), hi = nsteps - 2;
-    if (t < kVT) {
+    if (t < kVT && !L::BULK) {
+        // thread-stored rows; the two buffers alternate.  (Addressing them by
+        // step parity measured 3-4% faster than swapping pointers at K = 5, 6
+        // and 3% slower at K = 7.)
+        Bn = ring + BB;
         for (int i = 0; i < nsteps - 1; ++i) {
             const float x = xs[(i - rol) & 255];
-            vit_step<K, false>(f2, x, Bc, Bn, t, zr);
-            float* tmp = Bc; Bc = Bn; Bn = tmp;
-            const bool keep = i + 1 >= lo && i + 1 <= hi;
-            if (keep) row_fence_shared();       // this thread's writes -> async proxy
-            if (t == 0) row_copies_read();      // the previous row's source is free
+            float* grow = (i + 1 >= lo && i + 1 <= hi) ? rows + (size_t)(i + 1) * G::SPRE
+                                                       : nullptr;
+            if (K < 7) {
+                Bc = ring + (i & 1) * BB;
+                Bn = ring + ((i + 1) & 1) * BB;
+            }
+            vit_step<K, false>(f2, x, Bc, Bn, t, zr, grow);
+            if (K == 7) { float* tmp = Bc; Bc = Bn; Bn = tmp; }
             asm volatile("bar.sync 1, %0;" :: "r"(kVT) : "memory");
-            if (keep && t == 0)
-                row_copy(rows + (size_t)(i + 1) * G::SPRE, Bc, Lazy<K>::ROW_BYTES);
         }
+        Bc = ring + ((nsteps - 1) & 1) * BB;
+        Bn = ring + (nsteps & 1) * BB;
+    } else if (t < kVT) {
+        for (int i = 0; i < nsteps - 1; ++i) {
+            const float x = xs[(i - rol) & 255];
+            Bc = ring + (i & (L::RING - 1)) * BB;
+            Bn = ring + ((i + 1) & (L::RING - 1)) * BB;
+            const int q = i + 1;                  // the row this step writes
+            vit_step<K, false>(f2, x, Bc, Bn, t, zr);
+            const bool flush = q >= lo && q <= hi && ((q % L::BATCH) == L::BATCH - 1 || q == hi);
+            if (flush) row_fence_shared();        // this thread's writes -> async proxy
+            if (t == 0) row_copies_read();        // earlier copies have read their slots
+            asm volatile("bar.sync 1, %0;" :: "r"(kVT) : "memory");
+            if (flush && t == 0) {
+                const int first = max(q - q % L::BATCH, lo);
+                row_copy(rows + (size_t)first * G::SPRE, ring + (first & (L::RING - 1)) * BB,
+                         (q - first + 1) * L::ROW_BYTES);
+            }
+        }
+        Bc = ring + ((nsteps - 1) & (L::RING - 1)) * BB;
+        Bn = ring + (nsteps & (L::RING - 1)) * BB;
+    }
+    if (t < kVT) {
         // final step, untraced: best_n[j] = min_w cost_{n-1}(j + w 2^(16-K)).
         // The pass ends at the first-index argmin over cost_{n-1}: the lowest
         // state s = j + w 2^(16-K) whose cost is v* = min_j best_n[j] (pass 2:
@@ -295,7 +348,7 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
         if ((t & 31) == 0) reds[t >> 5] = bs;
         // the rows are in global memory before the pass ends (the next phase's
         // traceback reads them)
-        if (t == 0) row_copies_done();
+        if (L::BULK && t == 0) row_copies_done();
     } else {
         tb_job_run<K>(smem, lut32, t - kVT);
     }

@@ -301,10 +301,14 @@ __device__ __forceinline__ void vit_load_bin(const float* __restrict__ Bc, int m
 // One trellis step: best_{i+1} = min-plus over this thread's states using
 // best_i (Bc) and target x; writes best_{i+1} (Bn), returns packed argmins
 // (output e's argmin w in bits [e*BPE, e*BPE + BPE)); 0 when !TRACK.
+// grow (untraced steps of the slice geometries, K >= 4): also store this
+// thread's outputs to a global row in natural index order -- contiguous NJ
+// floats per thread, one or two vector stores.
 template <int K, bool TRACK = true>
 __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
                                              const float* __restrict__ Bc,
-                                             float* __restrict__ Bn, int t, float zr) {
+                                             float* __restrict__ Bn, int t, float zr,
+                                             float* __restrict__ grow = nullptr) {
     using G = Geo<K>;
     constexpr int NCH = G::NCH;
     constexpr int NJ = G::NJ;
@@ -340,6 +344,20 @@ __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
         }
 #pragma unroll
         for (int u = 0; u < NJ; ++u) Bn[G::baddr(G::out_j(t, b * NJ + u))] = outv[u];
+        if (!TRACK && !G::WHOLE && grow != nullptr) {
+            float* dst = grow + G::out_j(t, 0);
+            if (NJ >= 4) {
+#pragma unroll
+                for (int q = 0; q < NJ / 4; ++q)
+                    reinterpret_cast<float4*>(dst)[q] =
+                        make_float4(outv[(4 * q) % NJ], outv[(4 * q + 1) % NJ],
+                                    outv[(4 * q + 2) % NJ], outv[(4 * q + 3) % NJ]);
+            } else if (NJ == 2) {
+                *reinterpret_cast<float2*>(dst) = make_float2(outv[0], outv[1 % NJ]);
+            } else {
+                dst[0] = outv[0];
+            }
+        }
     }
     return bits;
 }
