@@ -37,7 +37,8 @@ struct LazySched {
 template <int K>
 struct LazyTileSmem {
     static constexpr int OFF_WX = LazySmem<K>::BYTES;           // 1 KB feedback staging
-    static constexpr int OFF_SCHED = OFF_WX + 1024;
+    static constexpr int OFF_GATHER = OFF_WX + 1024;            // feedback rows
+    static constexpr int OFF_SCHED = OFF_GATHER + kGatherStageBytes;
     static constexpr int BYTES = OFF_SCHED + (int)((sizeof(LazySched) + 15) / 16 * 16);
 };
 
@@ -122,6 +123,7 @@ ldlq_lazy_kernel(const __grid_constant__ LdlqTileParams p) {
     float* xs = reinterpret_cast<float*>(smem + SM::OFF_X);
     int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST);
     float* wx = reinterpret_cast<float*>(smem + TS::OFF_WX);
+    float* gst = reinterpret_cast<float*>(smem + TS::OFF_GATHER);
     volatile TbJob* jb = reinterpret_cast<volatile TbJob*>(smem + SM::OFF_JOB);
     volatile LazySched* sc = reinterpret_cast<volatile LazySched*>(smem + TS::OFF_SCHED);
     float* reg0 = p.lazy_ws + (size_t)(2 * blockIdx.x) * (L::REGION / 4);
@@ -166,7 +168,7 @@ ldlq_lazy_kernel(const __grid_constant__ LdlqTileParams p) {
             __syncthreads();
             if (!sc->ok) break;
         }
-        tile_feedback_gather(p, sc->i[0], sc->c[0], xs, wx, t);
+        tile_feedback_gather(p, sc->i[0], sc->c[0], xs, wx, gst, t, kLazyThreads);
 
         // ---- phase a: F1(A) | T2(previous B)
         if (t == 0 && sc->pend)
@@ -206,7 +208,7 @@ ldlq_lazy_kernel(const __grid_constant__ LdlqTileParams p) {
             if (!hasB) break;
             continue;
         }
-        tile_feedback_gather(p, sc->i[1], sc->c[1], xs + kSteps, wx, t);
+        tile_feedback_gather(p, sc->i[1], sc->c[1], xs + kSteps, wx, gst, t, kLazyThreads);
 
         // ---- phase b: F1(B) | T1(A)
         if (t == 0) tb_job_start<K>(smem, reg0, 0, 0, pivot, -1, pivot, n1 - 1, fA1);

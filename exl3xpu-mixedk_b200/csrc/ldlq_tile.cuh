@@ -77,32 +77,58 @@ __device__ __forceinline__ void tile_of_ticket(const LdlqTileParams& p, int tick
 
 // Feedback and gather of tile (i, c) into xs[256] (quantize.py:676-686):
 //   WXWX = (Wq + Lfac[later, blk]^T . E[later]) + prod,  x[t] = WXWX[perm[t]].
-// wx: 1 KB shared staging.  Every thread of the CTA calls it (two barriers).
+// The later rows r of this buffer (16 (i+1) <= r < 16 cur) are staged in
+// chunks of kGatherRows: every thread of the CTA issues coalesced 16-byte
+// loads of the rows' 16-wide slices Lfac[r, 16 i ..] and E[r, 16 c ..] (E
+// at L2, ld.global.cg: other CTAs of this launch wrote it), so a chunk costs
+// one memory round trip; then thread (a, col) accumulates
+// fma(Lfac[r, 16 i + a], E[r, 16 c + col], acc) over r ascending from
+// shared memory.  wx: 1 KB shared staging; stage: 2 x kGatherRows x 64 bytes
+// (16 KB), 16-byte aligned.  Every thread of the CTA (nthreads) calls it.
+constexpr int kGatherRows = 128;
+constexpr int kGatherStageBytes = 2 * kGatherRows * 16 * 4;
+
 __device__ __forceinline__ void tile_feedback_gather(const LdlqTileParams& p, int i, int c,
-                                                     float* xs, float* wx, int t) {
+                                                     float* xs, float* wx, float* stage,
+                                                     int t, int nthreads) {
     const int tn = p.seg_c0[p.nseg];
     const size_t n = (size_t)p.n;
+    const int a = (t >> 4) & 15, col = t & 15;
+    const size_t row = (size_t)(16 * i + a);
+    const size_t gc = (size_t)(16 * c + col);
+    float w = 0.0f, pr = 0.0f;
     if (t < 256) {
-        const int a = t >> 4, col = t & 15;
-        const size_t row = (size_t)(16 * i + a);
-        const size_t gc = (size_t)(16 * c + col);
-        float w = p.Wq[row * n + gc];
-        if (p.Lfac) {
-            const int r_lo = 16 * (i + 1), r_hi = 16 * p.cur;
-            if (r_lo < r_hi) {
-                // E rows of this buffer were written by other CTAs of this
-                // launch: read them at L2 (ld.global.cg), never from a
-                // possibly stale L1 line shared with a neighbouring column
-                float acc = 0.0f;
-                for (int r = r_lo; r < r_hi; ++r)
-                    acc = fmaf(p.Lfac[(size_t)r * p.k + 16 * i + a],
-                               __ldcg(&p.E[(size_t)r * n + gc]), acc);
-                w = w + acc;
-            }
-            w = w + p.prod[row * n + gc];
-        }
-        wx[t] = w;
+        w = p.Wq[row * n + gc];
+        if (p.Lfac) pr = p.prod[row * n + gc];
     }
+    if (p.Lfac) {
+        const int r_lo = 16 * (i + 1), r_hi = 16 * p.cur;
+        if (r_lo < r_hi) {
+            float acc = 0.0f;
+            float4* sL = reinterpret_cast<float4*>(stage);
+            float4* sE = sL + kGatherRows * 4;
+            for (int r0 = r_lo; r0 < r_hi; r0 += kGatherRows) {
+                const int nq = 4 * min(kGatherRows, r_hi - r0);   // float4 per slice set
+                for (int q = t; q < nq; q += nthreads) {
+                    const size_t r = (size_t)(r0 + (q >> 2));
+                    const int o = 4 * (q & 3);
+                    sL[q] = *reinterpret_cast<const float4*>(p.Lfac + r * p.k + 16 * i + o);
+                    sE[q] = __ldcg(reinterpret_cast<const float4*>(p.E + r * n + 16 * c + o));
+                }
+                __syncthreads();
+                if (t < 256) {
+                    const float* L = reinterpret_cast<const float*>(sL);
+                    const float* Ev = reinterpret_cast<const float*>(sE);
+                    for (int rr = 0; rr < nq / 4; ++rr)
+                        acc = fmaf(L[rr * 16 + a], Ev[rr * 16 + col], acc);
+                }
+                __syncthreads();
+            }
+            w = w + acc;
+        }
+        w = w + pr;
+    }
+    if (t < 256) wx[t] = w;
     __syncthreads();
     if (t < 256) {
         const float x = wx[tc_perm(t)];

@@ -225,6 +225,10 @@ int exl3b_u_to_gram(const float* dU, int k, double* dG, void* ws,
  *   dHatW [k][n] fp32 decoded weights (output)
  *   dStates [k/16][n/16][256] int32 (nullable), dXout [k/16][n/16][256]
  *         fp32 encoder targets (nullable; for per-launch checks)
+ *   buf_cols: the reference's LDLQ buffer (rows of k between feedback-cache
+ *         updates); launches cover max(buf_cols, 512) rows, the fastest
+ *         blocking here (the LDLQ targets are the same sums in another fp32
+ *         order)
  *   block_lo/block_hi: process k-blocks [block_lo, block_hi) (full sweep:
  *         0, k/16); successive calls must walk downwards with the same ws
  *   ws: exl3b_ldlq_workspace_bytes(k, n, min K, dLfac != NULL) bytes,

@@ -316,7 +316,8 @@ def test_stored_fields_dequantise_to_w_hat(xq, tmp_path):
 
 
 @pytest.mark.parametrize("k,n,K,buf_cols,pivot,margin", [
-    (256, 768, 4, 128, 128, 0),      # 8 x 48 = 384 tiles per buffer launch
+    (256, 768, 4, 128, 128, 0),      # one launch (512-row minimum): 16 x 48 tiles
+    (1024, 320, 5, 128, 7, 16),      # two 512-row launches, tcgen05 feedback between
     (256, 640, 5, 128, 7, 16),       # short first pass
     (256, 1184, 7, 128, 200, 100),
     (256, 768, 3, 128, 128, 0),      # whole-butterfly geometries (K = 2, 3)
