@@ -114,7 +114,7 @@ int launch_f32_to_f64(const float* a, double* b, size_t n, cudaStream_t stream);
 template <typename T>
 int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream_t stream,
               float* panel_ws = nullptr, int* gemm_err = nullptr);
-// fp32 scratch a block_ldl<float> trailing update on tensor cores needs (n x 64)
+// fp32 scratch a block_ldl<float> on tensor cores needs (transposed outer panel, 512 x n)
 size_t ldl_panel_bytes(int n);
 int u_to_gram_f64(const float* U, int n, double* Ud, double* Ui, double* G, cudaStream_t stream);
 int launch_gemm_tn_acc_f32(int M, int N, int K, const float* A_T, int lda,

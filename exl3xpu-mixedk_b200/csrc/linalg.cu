@@ -214,44 +214,75 @@ transpose_panel_kernel(const float* __restrict__ P, int ldp, int rows, int cols,
     }
 }
 
-size_t ldl_panel_bytes(int n) { return (size_t)kNB * n * sizeof(float); }
+// Outer panel of the two-level blocking (fp32 tensor-core path).
+constexpr int kOuterNB = 512;
 
-// Blocked right-looking Cholesky (panel kNB): diagonal block, panel solve,
-// trailing update A[j0+nb:, j0+nb:] -= P . P^T (P = A[j0+nb:, j0:j0+nb]).
-// fp32 with panel_ws: the trailing update runs on tcgen05 tensor cores
-// (3xTF32, gemm_tc.cu) from a transposed copy of the panel, over the 128 x 128
-// tiles that reach the lower triangle -- the entries above the diagonal that
-// the diagonal tiles also write are never read and are zeroed at the end.  fp64 (and fp32 without panel_ws): SIMT update of
-// the lower triangle.
+size_t ldl_panel_bytes(int n) { return (size_t)kOuterNB * ((n + 3) & ~3) * sizeof(float); }
+
+// Blocked right-looking Cholesky: diagonal block (kNB), panel solve, update.
+// fp32 with panel_ws (tcgen05 tensor cores, 3xTF32, gemm_tc.cu) blocks on two
+// levels, because a rank-64 update of the whole trailing matrix reads and
+// writes all of it for 64 columns of work (memory-bound: ~220 GB of traffic at
+// n = 17408):
+//  * inner steps of kNB columns inside an outer panel of kOuterNB columns:
+//    potrf, trsm of the rows below, and the rank-kNB update of the outer
+//    panel's remaining columns only;
+//  * one rank-kOuterNB update of the trailing matrix per outer panel
+//    (compute-bound; 8x less traffic).
+// Every inner panel P (rows below its diagonal block) is transposed once into
+// panel_ws [kOuterNB][ldt] (row = column within the outer panel, column =
+// global row - J); the inner updates and the outer update both read it.  The
+// GEMM covers the 128 x 128 tiles that reach the lower triangle -- the
+// entries above the diagonal that the diagonal tiles also write are never read
+// and are zeroed at the end.  fp64 (and fp32 without panel_ws): one level, SIMT
+// update of the lower triangle.
 template <typename T>
 int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_ws,
                    int* gemm_err) {
-    for (int j0 = 0; j0 < n; j0 += kNB) {
-        const int nb = (n - j0) < kNB ? (n - j0) : kNB;
-        potrf_diag_kernel<T><<<1, 1024, 0, stream>>>(A, n, j0, nb, dstatus);
-        const int rest = n - j0 - nb;
-        if (rest > 0) {
+    const bool tc = sizeof(T) == 4 && panel_ws != nullptr;
+    const int outer = tc ? kOuterNB : n;
+    const int ldt = (n + 3) & ~3;
+    for (int J = 0; J < n; J += outer) {
+        const int W = (n - J) < outer ? (n - J) : outer;
+        for (int j0 = J; j0 < J + W; j0 += kNB) {
+            const int nb = (J + W - j0) < kNB ? (J + W - j0) : kNB;
+            potrf_diag_kernel<T><<<1, 1024, 0, stream>>>(A, n, j0, nb, dstatus);
+            note_launch();
+            const int rest = n - j0 - nb;
+            if (rest <= 0) continue;
             trsm_panel_kernel<T><<<(rest + 127) / 128, 128, 0, stream>>>(A, n, j0, nb, dstatus);
+            note_launch();
+            const int wi = J + W - (j0 + nb);     // outer-panel columns right of this panel
             T* P = A + (size_t)(j0 + nb) * n + j0;
             T* C = A + (size_t)(j0 + nb) * n + (j0 + nb);
-            int rc;
-            if (sizeof(T) == 4 && panel_ws) {
-                const int ldt = (rest + 3) & ~3;
+            int rc = RC_OK;
+            if (tc) {
+                float* PT = panel_ws + (size_t)(j0 - J) * ldt + (j0 + nb - J);
                 dim3 g((rest + 31) / 32, (nb + 31) / 32);
                 transpose_panel_kernel<<<g, 256, 0, stream>>>(
-                    reinterpret_cast<const float*>(P), n, rest, nb, panel_ws, ldt);
+                    reinterpret_cast<const float*>(P), n, rest, nb, PT, ldt);
                 note_launch();
-                rc = launch_gemm_tn_acc_tc(rest, rest, nb, panel_ws, ldt, panel_ws, ldt,
-                                           reinterpret_cast<float*>(C), n, gemm_err, stream,
-                                           -1.0f, 1);
-            } else {
-                rc = gemm_launch<T, true, true, true>(rest, rest, nb, P, n, P, n, C, n,
-                                                      T(-1), T(1), dstatus, stream);
+                if (wi > 0)
+                    rc = launch_gemm_tn_acc_tc(rest, wi, nb, PT, ldt, PT, ldt,
+                                               reinterpret_cast<float*>(C), n, gemm_err,
+                                               stream, -1.0f, 1);
+            } else if (wi > 0) {
+                rc = gemm_launch<T, true, true, true>(rest, wi, nb, P, n, P, n, C, n, T(-1),
+                                                      T(1), dstatus, stream);
             }
             if (rc) return rc;
+            if (check_cuda(cudaGetLastError(), "cholesky launch")) return RC_DEVICE_ERROR;
         }
-        note_launch(rest > 0 ? 2 : 1);
-        if (check_cuda(cudaGetLastError(), "cholesky launch")) return RC_DEVICE_ERROR;
+        const int R = n - (J + W);
+        if (tc && R > 0) {
+            // A[J+W:, J+W:] -= Q Q^T, Q = A[J+W:, J:J+W] (transposed: panel_ws
+            // rows 0..W-1 from column W on)
+            const float* QT = panel_ws + W;
+            float* C = reinterpret_cast<float*>(A) + (size_t)(J + W) * n + (J + W);
+            const int rc = launch_gemm_tn_acc_tc(R, R, W, QT, ldt, QT, ldt, C, n, gemm_err,
+                                                 stream, -1.0f, 1);
+            if (rc) return rc;
+        }
     }
     zero_upper_kernel<T><<<1024, 256, 0, stream>>>(A, n);
     note_launch();
