@@ -117,14 +117,40 @@ __device__ __forceinline__ T dsqrt(T v);
 template <> __device__ __forceinline__ float dsqrt<float>(float v) { return sqrtf(v); }
 template <> __device__ __forceinline__ double dsqrt<double>(double v) { return sqrt(v); }
 
+// Inverse of the factored block in S (see potrf_diag_kernel), 1024 threads.
+__device__ __forceinline__ void potrf_inverse(const float (&S)[kNB][kNB + 1], int nb,
+                                              float* __restrict__ Linv, int t) {
+    using T = float;
+    __shared__ T X[kNB][kNB + 1];
+    const int c = t >> 4, q = t & 15;           // column, lane within its half-warp
+    for (int j = 0; j < kNB; ++j) {
+        const bool act = c < nb && j < nb && j >= c;
+        T part = T(0);
+        if (act)
+            for (int m = c + q; m < j; m += 16) part += S[j][m] * X[m][c];
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off, 16);
+        if (q == 0) X[j][c] = act ? ((j == c) ? T(1) / S[j][j] : -part / S[j][j]) : T(0);
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int idx = t; idx < kNB * kNB; idx += 1024) Linv[idx] = X[idx / kNB][idx % kNB];
+}
+
 // Factor the kNB x kNB diagonal block at (j0, j0) in place (lower).  1024
 // threads as 32 x 32; every thread derives the pivot's square root from
 // shared memory itself (the same value everywhere), so a column costs two
 // barriers: scale the column, then the rank-1 update of the trailing lower
 // triangle, 2-D strided without integer division.
+// Linv (optional, [kNB][kNB] row-major): also the inverse of the factored
+// block, lower triangular, zero above the diagonal (and outside nb x nb).
+// Column c of the inverse solves L x = e_c by forward substitution: 16
+// threads per column (one half-warp) split each step's sum and combine it
+// with shuffles, so the 64 steps need no block barrier.
 template <typename T>
 __global__ void __launch_bounds__(1024)
-potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ status) {
+potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ status,
+                  T* __restrict__ Linv = nullptr) {
     __shared__ T S[kNB][kNB + 1];
     if (*status) return;
     const int t = threadIdx.x;
@@ -152,6 +178,206 @@ potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ st
     }
     for (int r = ty; r < nb; r += 32)
         for (int c = tx; c <= r; c += 32) A[(size_t)(j0 + r) * n + (j0 + c)] = S[r][c];
+    if constexpr (sizeof(T) == 4) {             // the fp32 tensor-core path only
+        if (Linv != nullptr) potrf_inverse(S, nb, Linv, t);
+    }
+}
+
+
+// fp32, tensor-core path: factor the nb x nb diagonal block at (j0, j0) (nb a
+// multiple of 16, <= kNB) in place and write its inverse (lower triangular,
+// zero above the diagonal and outside nb x nb) to Linv [kNB][kNB].  Blocked by
+// 16 so that the serial work is warp-local: for each 16-column block K,
+//   (1) warp 0 factors the 16 x 16 diagonal block in registers (lane l holds
+//       row l; each column's values are broadcast with shuffles) and inverts
+//       it (lane c forward-substitutes column c in registers, multiplying by
+//       the diagonal's reciprocals);
+//   (2) the CTA solves the rows below against it: S[r, K] <- S[r, K] inv^T;
+//   (3) the CTA applies the rank-16 update to the trailing lower triangle.
+// Then the off-diagonal blocks of the inverse, row block by row block:
+//   V[I][J] = -inv(L_II) . sum_{K=J}^{I-1} L[I][K] V[K][J].
+// Records a LAPACK-style info (1-based column of the first non-positive /
+// non-finite pivot) in *status, like potrf_diag_kernel.  512 threads.
+__global__ void __launch_bounds__(512)
+potrf_inv_kernel(float* __restrict__ A, int n, int j0, int nb, int* __restrict__ status,
+                 float* __restrict__ Linv) {
+    __shared__ float S[kNB][kNB + 1];     // the block; becomes L (lower)
+    __shared__ float V[kNB][kNB + 1];     // the inverse
+    __shared__ float Tm[16][kNB + 1];     // one row block of partial products
+    __shared__ int bad_s;
+    if (*status) return;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int idx = t; idx < kNB * kNB; idx += 512) {
+        const int r = idx / kNB, c = idx % kNB;
+        S[r][c] = (r < nb && c <= r) ? A[(size_t)(j0 + r) * n + (j0 + c)] : 0.0f;
+        V[r][c] = 0.0f;
+    }
+    if (t == 0) bad_s = 0;
+    __syncthreads();
+    const int nblk = nb / 16;
+    for (int K = 0; K < nblk; ++K) {
+        const int k0 = 16 * K;
+        if (warp == 0) {
+            // lane l < 16 holds row l of the 16 x 16 diagonal block in registers
+            float a[16];
+#pragma unroll
+            for (int m = 0; m < 16; ++m) a[m] = (lane < 16) ? S[k0 + lane][k0 + m] : 0.0f;
+            int badj = -1;                           // the same in every lane
+#pragma unroll 16   // fully: a[] must stay in registers
+            for (int j = 0; j < 16; ++j) {
+                const float d = __shfl_sync(0xffffffffu, a[j], j);
+                const bool good = (d > 0.0f) && isfinite(d);
+                if (!good && badj < 0) badj = j;
+                const float djj = sqrtf(good ? d : 1.0f);
+                if (lane == j) a[j] = djj;
+                if (lane > j) a[j] = a[j] / djj;
+                // rank-1 update: a[c] -= a[j] * L[c][j] for j < c <= lane
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    if (c > j) {
+                        const float lcj = __shfl_sync(0xffffffffu, a[j], c);
+                        if (lane >= c) a[c] = fmaf(-a[j], lcj, a[c]);
+                    }
+                }
+            }
+            if (badj >= 0 && lane == 0) bad_s = j0 + k0 + badj + 1;
+            if (badj < 0) {
+                if (lane < 16) {
+#pragma unroll
+                    for (int m = 0; m < 16; ++m)
+                        if (m <= lane) S[k0 + lane][k0 + m] = a[m];
+                }
+                __syncwarp();
+                if (lane < 16) {     // column `lane` of the block's inverse
+                    const int c = lane;
+                    float rd[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) rd[j] = 1.0f / S[k0 + j][k0 + j];
+                    float x[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        float sacc = (j == c) ? 1.0f : 0.0f;
+#pragma unroll
+                        for (int m = 0; m < j; ++m) sacc = fmaf(-S[k0 + j][k0 + m], x[m], sacc);
+                        x[j] = (j < c) ? 0.0f : sacc * rd[j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) V[k0 + j][k0 + c] = x[j];
+                }
+            }
+        }
+        __syncthreads();
+        if (bad_s) break;
+        const int rb = nb - k0 - 16;          // rows below the block
+        if (rb > 0) {
+            float val[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int idx = t + 512 * q;
+                val[q] = 0.0f;
+                if (idx < rb * 16) {
+                    const int r = k0 + 16 + (idx >> 4), c = idx & 15;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int m = 0; m < 16; ++m) acc = fmaf(S[r][k0 + m], V[k0 + c][k0 + m], acc);
+                    val[q] = acc;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int idx = t + 512 * q;
+                if (idx < rb * 16) S[k0 + 16 + (idx >> 4)][k0 + (idx & 15)] = val[q];
+            }
+            __syncthreads();
+            for (int idx = t; idx < rb * rb; idx += 512) {
+                const int i = k0 + 16 + idx / rb, c = k0 + 16 + idx % rb;
+                if (c <= i) {
+                    float acc = S[i][c];
+#pragma unroll
+                    for (int m = 0; m < 16; ++m) acc = fmaf(-S[i][k0 + m], S[c][k0 + m], acc);
+                    S[i][c] = acc;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (bad_s) {
+        if (t == 0) *status = bad_s;
+        return;
+    }
+    for (int I = 1; I < nblk; ++I) {
+        const int i0 = 16 * I;
+        // Tm[r][c] = sum_{m = c_blk .. i0-1} L[i0 + r][m] V[m][c], c < i0
+        for (int idx = t; idx < 16 * i0; idx += 512) {
+            const int r = idx / i0, c = idx % i0;
+            float acc = 0.0f;
+            for (int m = 16 * (c / 16); m < i0; ++m) acc = fmaf(S[i0 + r][m], V[m][c], acc);
+            Tm[r][c] = acc;
+        }
+        __syncthreads();
+        for (int idx = t; idx < 16 * i0; idx += 512) {
+            const int r = idx / i0, c = idx % i0;
+            float acc = 0.0f;
+#pragma unroll
+            for (int m = 0; m <= 15; ++m) acc = fmaf(V[i0 + r][i0 + m], Tm[m][c], acc);
+            V[i0 + r][c] = -acc;
+        }
+        __syncthreads();
+    }
+    for (int idx = t; idx < kNB * kNB; idx += 512) {
+        const int r = idx / kNB, c = idx % kNB;
+        if (r < nb && c <= r) A[(size_t)(j0 + r) * n + (j0 + c)] = S[r][c];
+        Linv[idx] = (r < nb && c < nb) ? V[r][c] : 0.0f;
+    }
+}
+
+// fp32 panel solve for the tensor-core path: rows i >= j0+nb of the panel,
+// A[i, j0:j0+nb] <- A[i, j0:j0+nb] . Linv^T (Linv from potrf_diag_kernel), in
+// 64-row tiles through shared memory (4 x 4 outputs per thread, ascending
+// sum over the panel columns); writes the solved rows back in place and
+// transposed into PT (PT[c][i - (j0+nb)], row pitch ldt) for the update GEMM.
+__global__ void __launch_bounds__(256)
+panel_apply_kernel(float* __restrict__ A, int n, int j0, int nb,
+                   const float* __restrict__ Linv, float* __restrict__ PT, int ldt,
+                   const int* __restrict__ status) {
+    __shared__ float LI[kNB][kNB + 1];
+    __shared__ float B[kNB][kNB + 1];
+    if (*status) return;
+    const int t = threadIdx.x;
+    const int rest = n - j0 - nb;
+    const int r0 = blockIdx.x * kNB;
+    for (int idx = t; idx < kNB * kNB; idx += 256) {
+        const int r = idx / kNB, c = idx % kNB;
+        LI[r][c] = (r < nb && c < nb) ? Linv[idx] : 0.0f;
+        B[r][c] = (r0 + r < rest && c < nb) ? A[(size_t)(j0 + nb + r0 + r) * n + j0 + c] : 0.0f;
+    }
+    __syncthreads();
+    const int rb = 4 * (t >> 4), cb = t & 15;   // rows rb..rb+3, columns cb + 16 j
+    float acc[4][4] = {};
+    for (int m = 0; m < kNB; ++m) {
+        float bv[4], lv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) bv[i] = B[rb + i][m];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) lv[j] = LI[cb + 16 * j][m];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(bv[i], lv[j], acc[i][j]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) B[rb + i][cb + 16 * j] = acc[i][j];
+    __syncthreads();
+    for (int idx = t; idx < kNB * kNB; idx += 256) {
+        const int r = idx / kNB, c = idx % kNB;              // row-major, coalesced
+        if (r0 + r < rest && c < nb) A[(size_t)(j0 + nb + r0 + r) * n + j0 + c] = B[r][c];
+        const int c2 = idx / kNB, r2 = idx % kNB;            // transposed, coalesced
+        if (r0 + r2 < rest && c2 < nb) PT[(size_t)c2 * ldt + r0 + r2] = B[r2][c2];
+    }
 }
 
 // Rows i >= j0+nb: A[i, j0:j0+nb] <- A[i, j0:j0+nb] . L_jj^-T (forward
@@ -195,29 +421,13 @@ __global__ void zero_upper_kernel(T* __restrict__ A, int n) {
     }
 }
 
-// PT[c][r] = P[r][c] for the rows x cols panel P (row pitch ldp); PT row pitch
-// ldt.  32 x 32 tiles through shared memory (coalesced both ways).
-__global__ void __launch_bounds__(256)
-transpose_panel_kernel(const float* __restrict__ P, int ldp, int rows, int cols,
-                       float* __restrict__ PT, int ldt) {
-    __shared__ float tile[32][33];
-    const int r0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
-    for (int k = ty; k < 32; k += 8) {
-        const int r = r0 + k, c = c0 + tx;
-        tile[k][tx] = (r < rows && c < cols) ? P[(size_t)r * ldp + c] : 0.0f;
-    }
-    __syncthreads();
-    for (int k = ty; k < 32; k += 8) {
-        const int c = c0 + k, r = r0 + tx;
-        if (c < cols && r < rows) PT[(size_t)c * ldt + r] = tile[tx][k];
-    }
-}
-
 // Outer panel of the two-level blocking (fp32 tensor-core path).
 constexpr int kOuterNB = 512;
 
-size_t ldl_panel_bytes(int n) { return (size_t)kOuterNB * ((n + 3) & ~3) * sizeof(float); }
+// panel_ws: the transposed outer panel [kOuterNB][ldt], then Linv [kNB][kNB]
+size_t ldl_panel_bytes(int n) {
+    return ((size_t)kOuterNB * ((n + 3) & ~3) + (size_t)kNB * kNB) * sizeof(float);
+}
 
 // Blocked right-looking Cholesky: diagonal block (kNB), panel solve, update.
 // fp32 with panel_ws (tcgen05 tensor cores, 3xTF32, gemm_tc.cu) blocks on two
@@ -242,33 +452,40 @@ int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_
     const bool tc = sizeof(T) == 4 && panel_ws != nullptr;
     const int outer = tc ? kOuterNB : n;
     const int ldt = (n + 3) & ~3;
+    float* linv = tc ? panel_ws + (size_t)kOuterNB * ldt : nullptr;
     for (int J = 0; J < n; J += outer) {
         const int W = (n - J) < outer ? (n - J) : outer;
         for (int j0 = J; j0 < J + W; j0 += kNB) {
             const int nb = (J + W - j0) < kNB ? (J + W - j0) : kNB;
-            potrf_diag_kernel<T><<<1, 1024, 0, stream>>>(A, n, j0, nb, dstatus);
-            note_launch();
             const int rest = n - j0 - nb;
-            if (rest <= 0) continue;
-            trsm_panel_kernel<T><<<(rest + 127) / 128, 128, 0, stream>>>(A, n, j0, nb, dstatus);
+            if (tc)
+                potrf_inv_kernel<<<1, 512, 0, stream>>>(reinterpret_cast<float*>(A), n, j0, nb,
+                                                        dstatus, linv);
+            else
+                potrf_diag_kernel<T><<<1, 1024, 0, stream>>>(A, n, j0, nb, dstatus);
             note_launch();
+            if (rest <= 0) continue;
             const int wi = J + W - (j0 + nb);     // outer-panel columns right of this panel
             T* P = A + (size_t)(j0 + nb) * n + j0;
             T* C = A + (size_t)(j0 + nb) * n + (j0 + nb);
             int rc = RC_OK;
             if (tc) {
+                // solve and transpose in one pass (the diagonal block's inverse)
                 float* PT = panel_ws + (size_t)(j0 - J) * ldt + (j0 + nb - J);
-                dim3 g((rest + 31) / 32, (nb + 31) / 32);
-                transpose_panel_kernel<<<g, 256, 0, stream>>>(
-                    reinterpret_cast<const float*>(P), n, rest, nb, PT, ldt);
+                panel_apply_kernel<<<(rest + kNB - 1) / kNB, 256, 0, stream>>>(
+                    reinterpret_cast<float*>(A), n, j0, nb, linv, PT, ldt, dstatus);
                 note_launch();
                 if (wi > 0)
                     rc = launch_gemm_tn_acc_tc(rest, wi, nb, PT, ldt, PT, ldt,
                                                reinterpret_cast<float*>(C), n, gemm_err,
                                                stream, -1.0f, 1);
-            } else if (wi > 0) {
-                rc = gemm_launch<T, true, true, true>(rest, wi, nb, P, n, P, n, C, n, T(-1),
-                                                      T(1), dstatus, stream);
+            } else {
+                trsm_panel_kernel<T><<<(rest + 127) / 128, 128, 0, stream>>>(A, n, j0, nb,
+                                                                           dstatus);
+                note_launch();
+                if (wi > 0)
+                    rc = gemm_launch<T, true, true, true>(rest, wi, nb, P, n, P, n, C, n,
+                                                          T(-1), T(1), dstatus, stream);
             }
             if (rc) return rc;
             if (check_cuda(cudaGetLastError(), "cholesky launch")) return RC_DEVICE_ERROR;
