@@ -274,7 +274,7 @@ int exl3b_u_to_gram(const float* dU, int k, double* dG, void* ws, size_t ws_byte
 // Workspace: E [k][n] | prod [k][n] (LDLQ only) | backpointer slots |
 // control words (slot flags, per-column progress, ticket, error word) |
 // lazy-pipeline row regions (SMs x 2 x Lazy<K>::REGION, largest for the
-// smallest K of the sweep).
+// smallest K of the sweep) | (LDLQ) the feedback GEMM's pre-split operands.
 static int sweep_slots() { return device_sms() * ldlq_tile_max_resident_per_sm() + 16; }
 
 static size_t sweep_slot(const int* seg_K, int nseg) {
@@ -299,7 +299,8 @@ size_t exl3b_ldlq_workspace_bytes(int k, int n, int kmin, int use_ldlq) {
     const size_t kn = (size_t)k * n * 4;
     const size_t bp = (size_t)sweep_slots() * bp_slot_bytes(kmin);
     return align256(kn) + (use_ldlq ? align256(kn) : 0) + align256(bp) +
-           sweep_ctrl_bytes(n / 16) + sweep_lazy_bytes(kmin);
+           sweep_ctrl_bytes(n / 16) + sweep_lazy_bytes(kmin) +
+           (use_ldlq ? align256(gemm_split_bytes(k, n, k)) : 0);
 }
 
 int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nseg,
@@ -362,6 +363,10 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     w += align256((size_t)a.nslots * bp_slot_bytes(kmin));
     int* ctrl = reinterpret_cast<int*>(w);
     a.lazy_ws = reinterpret_cast<float*>(w + sweep_ctrl_bytes(tn));
+    if (dLfac) {
+        a.split_ws = w + sweep_ctrl_bytes(tn) + sweep_lazy_bytes(kmin);
+        a.split_bytes = align256(gemm_split_bytes(k, n, k));
+    }
     a.slots = ctrl;
     a.colprog = ctrl + a.nslots;
     a.tickets = a.colprog + tn;
@@ -400,6 +405,11 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     return RC_OK;
 }
 
+size_t exl3b_feedback_gemm_workspace_bytes(int M, int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return 0;
+    return 256 + gemm_split_bytes(M, N, K);
+}
+
 int exl3b_feedback_gemm(int M, int N, int K, const float* dA_T, int lda, const float* dB,
                         int ldb, float* dC, int ldc, void* ws, size_t ws_bytes, void* stream) {
     if (M < 0 || N < 0 || K < 0 || lda < M || ldb < N || ldc < N) {
@@ -416,7 +426,12 @@ int exl3b_feedback_gemm(int M, int N, int K, const float* dA_T, int lda, const f
     int* err = static_cast<int*>(ws);
     if (check_cuda(cudaMemsetAsync(err, 0, sizeof(int), s), "memset gemm status"))
         return RC_DEVICE_ERROR;
-    int rc = launch_gemm_tn_acc_tc(M, N, K, dA_T, lda, dB, ldb, dC, ldc, err, s);
+    // beyond the status word: the pre-split operand path when it fits
+    uint8_t* split = static_cast<uint8_t*>(ws) + 256;
+    const size_t split_bytes = ws_bytes - 256;
+    int rc = launch_gemm_tn_acc_tc(M, N, K, dA_T, lda, dB, ldb, dC, ldc, err, s, 1.0f, 0,
+                                   split_bytes >= gemm_split_bytes(M, N, K) ? split : nullptr,
+                                   split_bytes);
     if (rc) return rc;
     int h = 0;
     if (check_cuda(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, s),

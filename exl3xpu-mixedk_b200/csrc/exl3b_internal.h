@@ -121,7 +121,10 @@ int launch_gemm_tn_acc_f32(int M, int N, int K, const float* A_T, int lda,
                            const float* B, int ldb, float* C, int ldc, cudaStream_t stream);
 int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const float* B,
                           int ldb, float* C, int ldc, int* err, cudaStream_t stream,
-                          float sa = 1.0f, int lower = 0);
+                          float sa = 1.0f, int lower = 0, void* split_ws = nullptr,
+                          size_t split_bytes = 0);
+// scratch of the pre-split operand path of launch_gemm_tn_acc_tc
+size_t gemm_split_bytes(int M, int N, int K);
 
 // ------------------------------------------------------------ LDLQ sweep
 struct SweepArgs {
@@ -141,6 +144,8 @@ struct SweepArgs {
     uint8_t* bp_ws;
     size_t bp_slot;
     float* lazy_ws;          // lazy pipeline: SMs x 2 row regions (lazy_pipeline launches)
+    void* split_ws;          // feedback GEMM pre-split operands (null: per-tile split)
+    size_t split_bytes;
     int nslots;              // backpointer slots (> SM count)
     int* slots;              // [nslots] ownership flags (zero at sweep start)
     int* colprog;            // [tn] finished k-blocks per column (zero at start)

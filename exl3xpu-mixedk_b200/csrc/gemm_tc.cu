@@ -291,6 +291,190 @@ feedback_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                      :: "r"(tmem), "r"(kTN) : "memory");
 }
 
+// ------------------------------------------------- pre-split operand path
+// For updates with many output tiles the hi/lo split is done once per operand
+// instead of once per output tile: tf32_split_kernel writes X (stored [K][R],
+// R contiguous, row pitch ld) as hi / lo arrays [R][kp] (K contiguous, kp =
+// K rounded up to 32, zero padded), each value x (times `sign`) as
+// hi = tf32(x), lo = tf32(x - hi) -- the same split as split_row.  Then
+// gemm_tf32x3_kernel streams 128 x 32 boxes of the four arrays with TMA
+// (128-byte swizzle: the boxes land in the UMMA K-major canonical layout as
+// they are) through a kStages ring: thread 0 loads, thread 32 issues the
+// MMAs (lo.hi, hi.lo, hi.hi per 8-deep k step, as above) and commits each
+// stage back to the loader; all four warps run the same epilogue, which adds
+// sa * acc (sa = +-1: exact, and the same bits as splitting sa * A).
+constexpr int kStages = 3;
+constexpr int kSplitK = 512;                        // K per pre-split piece
+constexpr int kOpBox = 128 * kTK * 4;               // one 128 x 32 tf32 tile: 16 KB
+constexpr int kStage2 = 4 * kOpBox;                 // Ah | Al | Bh | Bl
+constexpr int kGemm2Smem = kStages * kStage2 + 128 + 1024;
+
+__global__ void __launch_bounds__(256)
+tf32_split_kernel(const float* __restrict__ X, int ld, int K, int R, float sign,
+                  float* __restrict__ hi, float* __restrict__ lo, int kp) {
+    __shared__ float tile[32][33];
+    const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
+    for (int i = ty; i < 32; i += 8) {
+        const int k = k0 + i, r = r0 + tx;
+        tile[i][tx] = (k < K && r < R) ? sign * X[(size_t)k * ld + r] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int r = r0 + i, k = k0 + tx;
+        if (r < R && k < kp) {
+            const float v = tile[tx][i];
+            const float h = tf32_round(v);
+            hi[(size_t)r * kp + k] = h;
+            lo[(size_t)r * kp + k] = tf32_round(v - h);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128, 1)
+gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
+                   const __grid_constant__ CUtensorMap tmAl,
+                   const __grid_constant__ CUtensorMap tmBh,
+                   const __grid_constant__ CUtensorMap tmBl,
+                   float* __restrict__ C, int ldc, int M, int N, int kp, float sa,
+                   int lower, int* __restrict__ err) {
+    extern __shared__ __align__(1024) uint8_t gsm_raw[];
+    uint8_t* gsm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + kStages * kStage2);
+    // bars[0..S): stage full (TMA);  bars[S..2S): stage empty (MMA commit);
+    // bars[2S]: all MMAs done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
+    if (lower && n0 > m0 + kTM - 1) return;
+    const uint32_t full0 = smem_u32(&bars[0]);
+    const uint32_t empty0 = smem_u32(&bars[kStages]);
+    const uint32_t done = smem_u32(&bars[2 * kStages]);
+    const int nchunks = kp / kTK;
+    if (t == 0) {
+        for (int i = 0; i < 2 * kStages + 1; ++i)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&bars[i])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(tmem_slot)), "r"(kTN) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    __shared__ int fail_s;
+    if (t == 0) fail_s = 0;
+    __syncthreads();
+
+    if (t == 0) {
+        // loader: chunk kc into stage kc % S once the MMAs of chunk kc - S are done
+        int issued = 0;
+        bool ok = true;
+        for (int kc = 0; kc < nchunks && ok; ++kc) {
+            const int s = kc % kStages, r = kc / kStages;
+            if (r > 0) ok = mbar_wait(empty0 + 8 * s, (r - 1) & 1);
+            if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
+            const uint32_t bar = full0 + 8 * s;
+            const uint32_t dst = smem_u32(gsm + s * kStage2);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                         :: "r"(bar), "r"(kStage2) : "memory");
+            tma_load_2d(dst, &tmAh, kc * kTK, m0, bar);
+            tma_load_2d(dst + kOpBox, &tmAl, kc * kTK, m0, bar);
+            tma_load_2d(dst + 2 * kOpBox, &tmBh, kc * kTK, n0, bar);
+            tma_load_2d(dst + 3 * kOpBox, &tmBl, kc * kTK, n0, bar);
+            issued = kc + 1;
+        }
+        if (!ok) {
+            atomicExch(&fail_s, 1);
+            // every issued load lands before the shared memory is released
+            for (int kc = 0; kc < issued; ++kc)
+                mbar_wait(full0 + 8 * (kc % kStages), (kc / kStages) & 1);
+        }
+    } else if (t == 32) {
+        // MMA issuer
+        int committed = 0;
+        bool ok = true;
+        for (int kc = 0; kc < nchunks; ++kc) {
+            const int s = kc % kStages, r = kc / kStages;
+            ok = mbar_wait(full0 + 8 * s, r & 1);
+            if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t aH = smem_u32(gsm + s * kStage2), aL = aH + kOpBox;
+            const uint32_t bH = aH + 2 * kOpBox, bL = aH + 3 * kOpBox;
+#pragma unroll
+            for (int kk = 0; kk < kTK / 8; ++kk) {
+                const uint32_t off = kk * 32;
+                umma_tf32(tmem, umma_desc_k_sw128(aL + off), umma_desc_k_sw128(bH + off),
+                          (kc > 0 || kk > 0) ? 1u : 0u);
+                umma_tf32(tmem, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bL + off), 1u);
+                umma_tf32(tmem, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bH + off), 1u);
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         :: "r"(empty0 + 8 * s) : "memory");
+            committed = kc + 1;
+        }
+        if (!ok) atomicExch(&fail_s, 1);
+        // the last commit tracks every earlier MMA of this thread
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     :: "r"(done) : "memory");
+        (void)committed;
+    }
+    // everyone: all MMAs complete (or abandoned)
+    bool ok = mbar_wait(done, 0);
+    if (__syncthreads_or(!ok || fail_s)) {
+        if (t == 0) atomicCAS(err, 0, 4);
+    } else {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int row = m0 + 32 * warp + lane;
+        const bool vec = ((ldc & 3) == 0) && ((((uintptr_t)C) & 15) == 0);
+#pragma unroll 1
+        for (int cc = 0; cc < kTN / 32; ++cc) {
+            uint32_t r[32];
+            const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16) + 32 * cc;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+                "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+                "[%32];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                  "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                  "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+                  "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                  "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]),
+                  "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (row < M) {
+                float* crow = C + (size_t)row * ldc + n0 + 32 * cc;
+                const int lim = N - (n0 + 32 * cc);
+                if (vec && lim >= 32) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        float4 c4 = *reinterpret_cast<float4*>(crow + j);
+                        c4.x += sa * __uint_as_float(r[j]);
+                        c4.y += sa * __uint_as_float(r[j + 1]);
+                        c4.z += sa * __uint_as_float(r[j + 2]);
+                        c4.w += sa * __uint_as_float(r[j + 3]);
+                        *reinterpret_cast<float4*>(crow + j) = c4;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < lim) crow[j] = crow[j] + sa * __uint_as_float(r[j]);
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                     :: "r"(tmem), "r"(kTN) : "memory");
+}
+
 // ---------------------------------------------------------------- host side
 // cuTensorMapEncodeTiled is a driver-API entry point; it is resolved at run
 // time through the runtime (no link dependency on libcuda, so the library also
@@ -335,18 +519,97 @@ static int encode_operand(CUtensorMap* map, const float* base, int inner, int ou
     return RC_OK;
 }
 
+static int encode_split(CUtensorMap* map, const float* base, int kp, int rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)kp * 4};
+    cuuint32_t box[2] = {(cuuint32_t)kTK, 128};
+    cuuint32_t estr[2] = {1, 1};
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return RC_DEVICE_ERROR;
+    }
+    const CUresult r = enc(
+        map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return RC_DEVICE_ERROR;
+    }
+    return RC_OK;
+}
+
+static int kp_of(int K) {
+    const int k = K < kSplitK ? K : kSplitK;
+    return (k + kTK - 1) / kTK * kTK;
+}
+
+size_t gemm_split_bytes(int M, int N, int K) {
+    return ((size_t)M + (size_t)N) * kp_of(K) * 8 + 1024;
+}
+
 // C[M][N] += sa * A_T^T . B on tcgen05 (A_T [K][M], B [K][N], both row-major
 // with leading dimensions lda / ldb; all pointers 16-byte aligned, lda / ldb
-// multiples of 4; sa = +-1, applied exactly in the split pass).  lower: skip
-// the 128 x 128 tiles entirely above the diagonal (symmetric updates that only
-// need C's lower triangle).  err: device word set to 4 on a barrier time-out.
+// multiples of 4; sa = +-1, applied exactly).  lower: skip the 128 x 128 tiles
+// entirely above the diagonal (symmetric updates that only need C's lower
+// triangle).  err: device word set to 4 on a barrier time-out.  split_ws (>=
+// gemm_split_bytes(M, N, K) bytes): the pre-split operand path; without it
+// the per-tile split kernel above.
 int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const float* B,
                           int ldb, float* C, int ldc, int* err, cudaStream_t stream,
-                          float sa, int lower) {
+                          float sa, int lower, void* split_ws, size_t split_bytes) {
     if (M <= 0 || N <= 0 || K <= 0) return RC_OK;
     if (((uintptr_t)A_T & 15) || ((uintptr_t)B & 15) || (lda & 3) || (ldb & 3)) {
         set_error("tcgen05 GEMM operands must be 16-byte aligned");
         return RC_BAD_REQUEST;
+    }
+    if (split_ws != nullptr && split_bytes >= gemm_split_bytes(M, N, K)) {
+        // pre-split path, K in pieces of kSplitK
+        static bool attr2[kMaxDevices] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!attr2[dev]) {
+            if (check_cuda(cudaFuncSetAttribute(gemm_tf32x3_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kGemm2Smem),
+                           "cudaFuncSetAttribute(gemm_tf32x3)"))
+                return RC_DEVICE_ERROR;
+            attr2[dev] = true;
+        }
+        // B the first N rows of A (the same matrix): B's split is A's first rows
+        const bool same = A_T == B && lda == ldb && N <= M;
+        float* base = reinterpret_cast<float*>(((uintptr_t)split_ws + 1023) & ~(uintptr_t)1023);
+        for (int k0 = 0; k0 < K; k0 += kSplitK) {
+            const int kk = (K - k0) < kSplitK ? (K - k0) : kSplitK;
+            const int kp = (kk + kTK - 1) / kTK * kTK;
+            float* Ah = base;
+            float* Al = Ah + (size_t)M * kp;
+            float* Bh = same ? Ah : Al + (size_t)M * kp;
+            float* Bl = same ? Al : Bh + (size_t)N * kp;
+            dim3 sg((M + 31) / 32, kp / 32);
+            tf32_split_kernel<<<sg, 256, 0, stream>>>(A_T + (size_t)k0 * lda, lda, kk, M, 1.0f,
+                                                      Ah, Al, kp);
+            note_launch();
+            if (!same) {
+                dim3 sg2((N + 31) / 32, kp / 32);
+                tf32_split_kernel<<<sg2, 256, 0, stream>>>(B + (size_t)k0 * ldb, ldb, kk, N,
+                                                           1.0f, Bh, Bl, kp);
+                note_launch();
+            }
+            CUtensorMap tAh, tAl, tBh, tBl;
+            int rc = encode_split(&tAh, Ah, kp, M);
+            if (!rc) rc = encode_split(&tAl, Al, kp, M);
+            if (!rc) rc = encode_split(&tBh, Bh, kp, N);
+            if (!rc) rc = encode_split(&tBl, Bl, kp, N);
+            if (rc) return rc;
+            dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
+            gemm_tf32x3_kernel<<<grid, 128, kGemm2Smem, stream>>>(tAh, tAl, tBh, tBl, C, ldc, M,
+                                                                 N, kp, sa, lower, err);
+            note_launch();
+            if (check_cuda(cudaGetLastError(), "gemm_tf32x3 launch")) return RC_DEVICE_ERROR;
+        }
+        return RC_OK;
     }
     CUtensorMap tmA, tmB;
     int rc = encode_operand(&tmA, A_T, M, K, lda);

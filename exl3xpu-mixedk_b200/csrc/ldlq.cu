@@ -282,7 +282,8 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
             rc = launch_gemm_tn_acc_tc(16 * lo, a.n, 16 * (cur - lo),
                                        a.Lfac + (size_t)16 * lo * a.k, a.k,
                                        a.E + (size_t)16 * lo * a.n, a.n,
-                                       a.prod, a.n, a.err, stream);
+                                       a.prod, a.n, a.err, stream, 1.0f, 0,
+                                       a.split_ws, a.split_bytes);
             prof_end_launch(stream);
             if (rc) return rc;
         }

@@ -424,9 +424,13 @@ __global__ void zero_upper_kernel(T* __restrict__ A, int n) {
 // Outer panel of the two-level blocking (fp32 tensor-core path).
 constexpr int kOuterNB = 512;
 
-// panel_ws: the transposed outer panel [kOuterNB][ldt], then Linv [kNB][kNB]
+// panel_ws: the transposed outer panel [kOuterNB][ldt], Linv [kNB][kNB], then
+// the update GEMM's pre-split operands
+static size_t ldl_panel_floats(int n) {
+    return (size_t)kOuterNB * ((n + 3) & ~3) + (size_t)kNB * kNB;
+}
 size_t ldl_panel_bytes(int n) {
-    return ((size_t)kOuterNB * ((n + 3) & ~3) + (size_t)kNB * kNB) * sizeof(float);
+    return ldl_panel_floats(n) * sizeof(float) + gemm_split_bytes(n, n, kOuterNB);
 }
 
 // Blocked right-looking Cholesky: diagonal block (kNB), panel solve, update.
@@ -453,6 +457,8 @@ int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_
     const int outer = tc ? kOuterNB : n;
     const int ldt = (n + 3) & ~3;
     float* linv = tc ? panel_ws + (size_t)kOuterNB * ldt : nullptr;
+    void* split = tc ? static_cast<void*>(panel_ws + ldl_panel_floats(n)) : nullptr;
+    const size_t split_bytes = tc ? gemm_split_bytes(n, n, kOuterNB) : 0;
     for (int J = 0; J < n; J += outer) {
         const int W = (n - J) < outer ? (n - J) : outer;
         for (int j0 = J; j0 < J + W; j0 += kNB) {
@@ -478,7 +484,7 @@ int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_
                 if (wi > 0)
                     rc = launch_gemm_tn_acc_tc(rest, wi, nb, PT, ldt, PT, ldt,
                                                reinterpret_cast<float*>(C), n, gemm_err,
-                                               stream, -1.0f, 1);
+                                               stream, -1.0f, 1, split, split_bytes);
             } else {
                 trsm_panel_kernel<T><<<(rest + 127) / 128, 128, 0, stream>>>(A, n, j0, nb,
                                                                            dstatus);
@@ -497,7 +503,7 @@ int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_
             const float* QT = panel_ws + W;
             float* C = reinterpret_cast<float*>(A) + (size_t)(J + W) * n + (J + W);
             const int rc = launch_gemm_tn_acc_tc(R, R, W, QT, ldt, QT, ldt, C, n, gemm_err,
-                                                 stream, -1.0f, 1);
+                                                 stream, -1.0f, 1, split, split_bytes);
             if (rc) return rc;
         }
     }

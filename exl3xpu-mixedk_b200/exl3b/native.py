@@ -62,6 +62,7 @@ SIGNATURES = {
     "exl3b_ldlq_workspace_bytes": (SZ, [I, I, I, I]),
     "exl3b_ldlq_sweep": (I, [P, P, I, I, I, P, P, P, I, I, I, I, P, P, P, I, I,
                              P, SZ, P]),
+    "exl3b_feedback_gemm_workspace_bytes": (SZ, [I, I, I]),
     "exl3b_feedback_gemm": (I, [I, I, I, P, I, P, I, P, I, P, SZ, P]),
     "exl3b_pack_states": (I, [P, I, I, P, P]),
     "exl3b_unpack_states": (I, [P, I, I, P, P]),

@@ -244,8 +244,12 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
 /* LDLQ feedback-cache update (quantize.py:742-744) on tcgen05 tensor cores:
  *   C[M][N] += A_T^T . B,   A_T [K][M] (row pitch lda), B [K][N] (pitch ldb)
  * 3xTF32 (fp32-grade) products, TMA-fed, fp32 accumulation.  Pointers 16-byte
- * aligned, lda / ldb multiples of 4.  ws: >= 256 bytes of device scratch for a
- * status word.  Synchronises `stream`. */
+ * aligned, lda / ldb multiples of 4.  ws: >= 256 bytes of device scratch (a
+ * status word).  With exl3b_feedback_gemm_workspace_bytes(M, N, K) bytes the
+ * operands are split into tf32 hi / lo once per call (K in pieces of 512)
+ * instead of once per output tile: the same products, faster when there are
+ * many output tiles.  Synchronises `stream`. */
+size_t exl3b_feedback_gemm_workspace_bytes(int M, int N, int K);
 int exl3b_feedback_gemm(int M, int N, int K, const float* dA_T, int lda, const float* dB,
                         int ldb, float* dC, int ldc, void* ws, size_t ws_bytes,
                         void* stream);

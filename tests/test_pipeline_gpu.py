@@ -254,25 +254,51 @@ def test_sweep_with_more_tiles_than_resident_ctas(xq, oracle, mul1_lut):
     assert torch.equal(dec, hatW)
 
 
+def _gemm(M, N, K, A, lda, B, ldb, C, presplit):
+    from exl3b import native
+    L = native.lib()
+    nb = L.exl3b_feedback_gemm_workspace_bytes(M, N, K) if presplit else 256
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    native.call("exl3b_feedback_gemm", M, N, K, A.data_ptr(), lda, B.data_ptr(), ldb,
+                C.data_ptr(), N, ws.data_ptr(), nb, None)
+
+
+@pytest.mark.parametrize("presplit", (False, True))
 @pytest.mark.parametrize("M,N,K", [(300, 200, 128), (128, 128, 32), (5104, 5120, 128),
-                                   (64, 1024, 80)])
-def test_feedback_gemm_tcgen05(M, N, K):
+                                   (64, 1024, 80), (700, 333, 1100)])
+def test_feedback_gemm_tcgen05(M, N, K, presplit):
     """The tensor-core feedback update C += A_T^T B (3xTF32) against an fp64
     torch reference: fp32-grade accuracy, partial tiles, K not a multiple of
-    32 (zero-filled TMA boxes)."""
-    from exl3b import native
+    32 (zero-filled TMA boxes); per-tile split and pre-split operands (K in
+    pieces of 512)."""
     gen = torch.Generator(device="cuda").manual_seed(M + N + K)
-    lda, ldb = M + 20, N + 12
+    lda, ldb = (M + 23) // 4 * 4, (N + 15) // 4 * 4     # pitches: multiples of 4
     A = torch.randn(K, lda, device="cuda", generator=gen)
     B = torch.randn(K, ldb, device="cuda", generator=gen)
     C = torch.randn(M, N, device="cuda", generator=gen)
     ref = C.double() + A[:, :M].double().t() @ B[:, :N].double()
-    ws = torch.empty(256, dtype=torch.uint8, device="cuda")
-    native.call("exl3b_feedback_gemm", M, N, K, A.data_ptr(), lda, B.data_ptr(), ldb,
-                C.data_ptr(), N, ws.data_ptr(), 256, None)
+    _gemm(M, N, K, A, lda, B, ldb, C, presplit)
     err = (C.double() - ref).abs().max().item()
     scale = (A[:, :M].double().abs().t() @ B[:, :N].double().abs()).max().item()
-    assert err <= 2e-6 * scale, (err, scale)
+    # fp32 accumulation: the bound grows with the number of k terms
+    assert err <= 2e-6 * max(1.0, K / 128) * scale, (err, scale)
+
+
+@pytest.mark.parametrize("M,N,K,shared", [(300, 200, 128, False), (1000, 1000, 512, True),
+                                          (640, 200, 96, True), (129, 257, 33, False)])
+def test_feedback_gemm_presplit_bit_exact(M, N, K, shared):
+    """For K <= 512 the pre-split path feeds the MMAs the same tf32 hi / lo
+    values in the same order as the per-tile split: identical C, also when B
+    is the first N rows of A (one shared split, as in the LDL updates)."""
+    gen = torch.Generator(device="cuda").manual_seed(7 * M + N + K)
+    lda, ldb = (M + 7) // 4 * 4, (N + 11) // 4 * 4      # pitches: multiples of 4
+    A = torch.randn(K, lda, device="cuda", generator=gen)
+    B, ldb = (A, lda) if shared else (torch.randn(K, ldb, device="cuda", generator=gen), ldb)
+    C0 = torch.randn(M, N, device="cuda", generator=gen)
+    C1 = C0.clone()
+    _gemm(M, N, K, A, lda, B, ldb, C0, False)
+    _gemm(M, N, K, A, lda, B, ldb, C1, True)
+    assert torch.equal(C0, C1)
 
 
 @pytest.mark.parametrize("channel_scales", (False, True))
