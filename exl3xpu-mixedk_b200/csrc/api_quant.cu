@@ -226,11 +226,24 @@ int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
     if (check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "memset status") ||
         (gerr && check_cuda(cudaMemsetAsync(gerr, 0, sizeof(int), s), "memset gemm status")))
         return RC_DEVICE_ERROR;
+    // the lookahead's helper stream and events (per device, created once)
+    if (!f64 && !st->side) {
+        int lo_pri = 0, hi_pri = 0;
+        cudaDeviceGetStreamPriorityRange(&lo_pri, &hi_pri);
+        if (check_cuda(cudaStreamCreateWithPriority(&st->side, cudaStreamNonBlocking, hi_pri),
+                       "lookahead stream") ||
+            check_cuda(cudaEventCreateWithFlags(&st->ev_fork, cudaEventDisableTiming),
+                       "lookahead event") ||
+            check_cuda(cudaEventCreateWithFlags(&st->ev_join, cudaEventDisableTiming),
+                       "lookahead event"))
+            return RC_DEVICE_ERROR;
+    }
     prof_begin_launch(s, PROF_LDL, (double)k * k * k / 3.0);
     int rc = f64 ? block_ldl<double>(static_cast<double*>(dA), k, dLfac, static_cast<double*>(dD),
                                      static_cast<double*>(dli), status, s)
                  : block_ldl<float>(static_cast<float*>(dA), k, dLfac, static_cast<float*>(dD),
-                                    static_cast<float*>(dli), status, s, panel, gerr);
+                                    static_cast<float*>(dli), status, s, panel, gerr, st->side,
+                                    st->ev_fork, st->ev_join);
     prof_end_launch(s);
     if (rc) return rc;
     int h = 0, g = 0;

@@ -24,6 +24,9 @@ struct DeviceState {
     float* stageX = nullptr;          // xtq_vit_run staging (grow-only)
     int32_t* stageS = nullptr;
     size_t stage_seqs = 0;
+    // block LDL lookahead: a high-priority helper stream and fork / join events
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 };
 
 // Kernel-launch accounting (exl3b_launch_count) and optional per-launch
@@ -111,10 +114,15 @@ int launch_chan_store(const float* su, const float* r_in, const float* wscale,
 int launch_f32_to_f64(const float* a, double* b, size_t n, cudaStream_t stream);
 
 // ------------------------------------------------------------ factorisation
+// side / ev_fork / ev_join (optional, fp32 tensor-core path): a helper stream
+// and two events for the lookahead that overlaps each outer panel's trailing
+// update with the next panel's factorisation
 template <typename T>
 int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream_t stream,
-              float* panel_ws = nullptr, int* gemm_err = nullptr);
-// fp32 scratch a block_ldl<float> on tensor cores needs (transposed outer panel, 512 x n)
+              float* panel_ws = nullptr, int* gemm_err = nullptr, cudaStream_t side = nullptr,
+              cudaEvent_t ev_fork = nullptr, cudaEvent_t ev_join = nullptr);
+// fp32 scratch a block_ldl<float> on tensor cores needs (transposed outer panel
+// 512 x n, the diagonal block's inverse, the update GEMMs' pre-split operands)
 size_t ldl_panel_bytes(int n);
 int u_to_gram_f64(const float* U, int n, double* Ud, double* Ui, double* G, cudaStream_t stream);
 int launch_gemm_tn_acc_f32(int M, int N, int K, const float* A_T, int lda,
@@ -125,6 +133,14 @@ int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const 
                           size_t split_bytes = 0);
 // scratch of the pre-split operand path of launch_gemm_tn_acc_tc
 size_t gemm_split_bytes(int M, int N, int K);
+// the pre-split path in two steps: X [K][R] (pitch ld, K <= 512) -> tf32 hi / lo
+// [R][kp] (kp = K rounded up to 32; arrays 16-byte aligned), then
+// C[M][N] += sa * A.B^T over such arrays (rows of A and B: M and N)
+int gemm_split(const float* X, int ld, int K, int R, float* hi, float* lo, int kp,
+               cudaStream_t stream);
+int gemm_presplit_run(int M, int N, int kp, const float* Ah, const float* Al, const float* Bh,
+                      const float* Bl, float* C, int ldc, float sa, int lower, int* err,
+                      cudaStream_t stream);
 
 // ------------------------------------------------------------ LDLQ sweep
 struct SweepArgs {

@@ -549,6 +549,42 @@ size_t gemm_split_bytes(int M, int N, int K) {
     return ((size_t)M + (size_t)N) * kp_of(K) * 8 + 1024;
 }
 
+int gemm_split(const float* X, int ld, int K, int R, float* hi, float* lo, int kp,
+               cudaStream_t stream) {
+    dim3 g((R + 31) / 32, kp / 32);
+    tf32_split_kernel<<<g, 256, 0, stream>>>(X, ld, K, R, 1.0f, hi, lo, kp);
+    note_launch();
+    return check_cuda(cudaGetLastError(), "tf32_split launch") ? RC_DEVICE_ERROR : RC_OK;
+}
+
+int gemm_presplit_run(int M, int N, int kp, const float* Ah, const float* Al, const float* Bh,
+                      const float* Bl, float* C, int ldc, float sa, int lower, int* err,
+                      cudaStream_t stream) {
+    if (M <= 0 || N <= 0) return RC_OK;
+    static bool attr[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev]) {
+        if (check_cuda(cudaFuncSetAttribute(gemm_tf32x3_kernel,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kGemm2Smem),
+                       "cudaFuncSetAttribute(gemm_tf32x3)"))
+            return RC_DEVICE_ERROR;
+        attr[dev] = true;
+    }
+    CUtensorMap tAh, tAl, tBh, tBl;
+    int rc = encode_split(&tAh, Ah, kp, M);
+    if (!rc) rc = encode_split(&tAl, Al, kp, M);
+    if (!rc) rc = encode_split(&tBh, Bh, kp, N);
+    if (!rc) rc = encode_split(&tBl, Bl, kp, N);
+    if (rc) return rc;
+    dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
+    gemm_tf32x3_kernel<<<grid, 128, kGemm2Smem, stream>>>(tAh, tAl, tBh, tBl, C, ldc, M, N, kp,
+                                                         sa, lower, err);
+    note_launch();
+    return check_cuda(cudaGetLastError(), "gemm_tf32x3 launch") ? RC_DEVICE_ERROR : RC_OK;
+}
+
 // C[M][N] += sa * A_T^T . B on tcgen05 (A_T [K][M], B [K][N], both row-major
 // with leading dimensions lda / ldb; all pointers 16-byte aligned, lda / ldb
 // multiples of 4; sa = +-1, applied exactly).  lower: skip the 128 x 128 tiles
@@ -566,17 +602,6 @@ int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const 
     }
     if (split_ws != nullptr && split_bytes >= gemm_split_bytes(M, N, K)) {
         // pre-split path, K in pieces of kSplitK
-        static bool attr2[kMaxDevices] = {};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (!attr2[dev]) {
-            if (check_cuda(cudaFuncSetAttribute(gemm_tf32x3_kernel,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                kGemm2Smem),
-                           "cudaFuncSetAttribute(gemm_tf32x3)"))
-                return RC_DEVICE_ERROR;
-            attr2[dev] = true;
-        }
         // B the first N rows of A (the same matrix): B's split is A's first rows
         const bool same = A_T == B && lda == ldb && N <= M;
         float* base = reinterpret_cast<float*>(((uintptr_t)split_ws + 1023) & ~(uintptr_t)1023);
@@ -587,27 +612,10 @@ int launch_gemm_tn_acc_tc(int M, int N, int K, const float* A_T, int lda, const 
             float* Al = Ah + (size_t)M * kp;
             float* Bh = same ? Ah : Al + (size_t)M * kp;
             float* Bl = same ? Al : Bh + (size_t)N * kp;
-            dim3 sg((M + 31) / 32, kp / 32);
-            tf32_split_kernel<<<sg, 256, 0, stream>>>(A_T + (size_t)k0 * lda, lda, kk, M, 1.0f,
-                                                      Ah, Al, kp);
-            note_launch();
-            if (!same) {
-                dim3 sg2((N + 31) / 32, kp / 32);
-                tf32_split_kernel<<<sg2, 256, 0, stream>>>(B + (size_t)k0 * ldb, ldb, kk, N,
-                                                           1.0f, Bh, Bl, kp);
-                note_launch();
-            }
-            CUtensorMap tAh, tAl, tBh, tBl;
-            int rc = encode_split(&tAh, Ah, kp, M);
-            if (!rc) rc = encode_split(&tAl, Al, kp, M);
-            if (!rc) rc = encode_split(&tBh, Bh, kp, N);
-            if (!rc) rc = encode_split(&tBl, Bl, kp, N);
+            int rc = gemm_split(A_T + (size_t)k0 * lda, lda, kk, M, Ah, Al, kp, stream);
+            if (!rc && !same) rc = gemm_split(B + (size_t)k0 * ldb, ldb, kk, N, Bh, Bl, kp, stream);
+            if (!rc) rc = gemm_presplit_run(M, N, kp, Ah, Al, Bh, Bl, C, ldc, sa, lower, err, stream);
             if (rc) return rc;
-            dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
-            gemm_tf32x3_kernel<<<grid, 128, kGemm2Smem, stream>>>(tAh, tAl, tBh, tBl, C, ldc, M,
-                                                                 N, kp, sa, lower, err);
-            note_launch();
-            if (check_cuda(cudaGetLastError(), "gemm_tf32x3 launch")) return RC_DEVICE_ERROR;
         }
         return RC_OK;
     }

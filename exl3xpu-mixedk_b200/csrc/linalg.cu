@@ -424,13 +424,16 @@ __global__ void zero_upper_kernel(T* __restrict__ A, int n) {
 // Outer panel of the two-level blocking (fp32 tensor-core path).
 constexpr int kOuterNB = 512;
 
-// panel_ws: the transposed outer panel [kOuterNB][ldt], Linv [kNB][kNB], then
-// the update GEMM's pre-split operands
+// panel_ws: the transposed outer panel [kOuterNB][ldt], Linv [kNB][kNB], the
+// outer update's pre-split panel (one matrix: both operands), then the inner
+// updates' pre-split operands
 static size_t ldl_panel_floats(int n) {
     return (size_t)kOuterNB * ((n + 3) & ~3) + (size_t)kNB * kNB;
 }
+static size_t ldl_outer_split_bytes(int n) { return (size_t)n * kOuterNB * 8 + 1024; }
 size_t ldl_panel_bytes(int n) {
-    return ldl_panel_floats(n) * sizeof(float) + gemm_split_bytes(n, n, kOuterNB);
+    return ldl_panel_floats(n) * sizeof(float) + ldl_outer_split_bytes(n) +
+           gemm_split_bytes(n, kOuterNB, kNB);
 }
 
 // Blocked right-looking Cholesky: diagonal block (kNB), panel solve, update.
@@ -446,29 +449,50 @@ size_t ldl_panel_bytes(int n) {
 // Every inner panel P (rows below its diagonal block) is transposed once into
 // panel_ws [kOuterNB][ldt] (row = column within the outer panel, column =
 // global row - J); the inner updates and the outer update both read it.  The
+// outer update runs in two parts: the next outer panel's columns first, then
+// the rest.  With a helper stream `side` (high priority) the serial chain runs
+// there and the rest-updates on the caller's stream, so a rest-update overlaps
+// the next panel's diagonal steps; the update after it waits for it.  The
 // GEMM covers the 128 x 128 tiles that reach the lower triangle -- the
 // entries above the diagonal that the diagonal tiles also write are never read
 // and are zeroed at the end.  fp64 (and fp32 without panel_ws): one level, SIMT
 // update of the lower triangle.
 template <typename T>
 int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_ws,
-                   int* gemm_err) {
+                   int* gemm_err, cudaStream_t side, cudaEvent_t ev_fork,
+                   cudaEvent_t ev_join) {
     const bool tc = sizeof(T) == 4 && panel_ws != nullptr;
     const int outer = tc ? kOuterNB : n;
     const int ldt = (n + 3) & ~3;
     float* linv = tc ? panel_ws + (size_t)kOuterNB * ldt : nullptr;
-    void* split = tc ? static_cast<void*>(panel_ws + ldl_panel_floats(n)) : nullptr;
-    const size_t split_bytes = tc ? gemm_split_bytes(n, n, kOuterNB) : 0;
+    float* osplit = nullptr;
+    void* isplit = nullptr;
+    size_t isplit_bytes = 0;
+    if (tc) {
+        uint8_t* p = reinterpret_cast<uint8_t*>(panel_ws + ldl_panel_floats(n));
+        osplit = reinterpret_cast<float*>(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
+        isplit = p + ldl_outer_split_bytes(n);
+        isplit_bytes = gemm_split_bytes(n, kOuterNB, kNB);
+    }
+    // lookahead: the serial chain (diagonal steps, splits, next-panel updates)
+    // runs on the high-priority helper stream `side`, the rest-updates on the
+    // caller's stream, so that freed SMs go to the chain first
+    const bool ahead = tc && side && ev_fork && ev_join;
+    cudaStream_t cs = ahead ? side : stream;
+    bool pending = false;                     // a rest-update is in flight on `stream`
+    if (ahead && (check_cuda(cudaEventRecord(ev_join, stream), "lookahead start") ||
+                  check_cuda(cudaStreamWaitEvent(cs, ev_join, 0), "lookahead start")))
+        return RC_DEVICE_ERROR;
     for (int J = 0; J < n; J += outer) {
         const int W = (n - J) < outer ? (n - J) : outer;
         for (int j0 = J; j0 < J + W; j0 += kNB) {
             const int nb = (J + W - j0) < kNB ? (J + W - j0) : kNB;
             const int rest = n - j0 - nb;
             if (tc)
-                potrf_inv_kernel<<<1, 512, 0, stream>>>(reinterpret_cast<float*>(A), n, j0, nb,
-                                                        dstatus, linv);
+                potrf_inv_kernel<<<1, 512, 0, cs>>>(reinterpret_cast<float*>(A), n, j0, nb,
+                                                    dstatus, linv);
             else
-                potrf_diag_kernel<T><<<1, 1024, 0, stream>>>(A, n, j0, nb, dstatus);
+                potrf_diag_kernel<T><<<1, 1024, 0, cs>>>(A, n, j0, nb, dstatus);
             note_launch();
             if (rest <= 0) continue;
             const int wi = J + W - (j0 + nb);     // outer-panel columns right of this panel
@@ -478,13 +502,13 @@ int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_
             if (tc) {
                 // solve and transpose in one pass (the diagonal block's inverse)
                 float* PT = panel_ws + (size_t)(j0 - J) * ldt + (j0 + nb - J);
-                panel_apply_kernel<<<(rest + kNB - 1) / kNB, 256, 0, stream>>>(
+                panel_apply_kernel<<<(rest + kNB - 1) / kNB, 256, 0, cs>>>(
                     reinterpret_cast<float*>(A), n, j0, nb, linv, PT, ldt, dstatus);
                 note_launch();
                 if (wi > 0)
                     rc = launch_gemm_tn_acc_tc(rest, wi, nb, PT, ldt, PT, ldt,
                                                reinterpret_cast<float*>(C), n, gemm_err,
-                                               stream, -1.0f, 1, split, split_bytes);
+                                               cs, -1.0f, 1, isplit, isplit_bytes);
             } else {
                 trsm_panel_kernel<T><<<(rest + 127) / 128, 128, 0, stream>>>(A, n, j0, nb,
                                                                            dstatus);
@@ -498,15 +522,51 @@ int cholesky_lower(T* A, int n, int* dstatus, cudaStream_t stream, float* panel_
         }
         const int R = n - (J + W);
         if (tc && R > 0) {
-            // A[J+W:, J+W:] -= Q Q^T, Q = A[J+W:, J:J+W] (transposed: panel_ws
-            // rows 0..W-1 from column W on)
-            const float* QT = panel_ws + W;
-            float* C = reinterpret_cast<float*>(A) + (size_t)(J + W) * n + (J + W);
-            const int rc = launch_gemm_tn_acc_tc(R, R, W, QT, ldt, QT, ldt, C, n, gemm_err,
-                                                 stream, -1.0f, 1, split, split_bytes);
+            // A[J+W:, J+W:] -= Q Q^T, Q = A[J+W:, J:J+W] (transposed: panel_ws rows
+            // 0..W-1 from column W on), split once into osplit.  The previous
+            // rest-update reads osplit and writes the columns this one does:
+            // wait for it first.
+            if (pending && check_cuda(cudaStreamWaitEvent(cs, ev_join, 0), "lookahead join"))
+                return RC_DEVICE_ERROR;
+            pending = false;
+            const int kp = (W + 31) / 32 * 32;
+            float* Qh = osplit;
+            float* Ql = osplit + (size_t)R * kp;
+            int rc = gemm_split(panel_ws + W, ldt, W, R, Qh, Ql, kp, cs);
             if (rc) return rc;
+            float* Cf = reinterpret_cast<float*>(A);
+            // (a) the next outer panel's columns, rows J+W.. (its diagonal block
+            //     lower triangle + everything below), on the caller's stream
+            const int W2 = R < outer ? R : outer;
+            rc = gemm_presplit_run(R, W2, kp, Qh, Ql, Qh, Ql, Cf + (size_t)(J + W) * n + (J + W),
+                                   n, -1.0f, 1, gemm_err, cs);
+            if (rc) return rc;
+            // (b) the rest of the trailing matrix (columns >= J+W+W2), on the
+            //     caller's stream: it overlaps the next outer panel's diagonal
+            //     steps, which touch columns < J+W+W2 only
+            const int R2 = R - W2;
+            if (R2 > 0) {
+                if (ahead && (check_cuda(cudaEventRecord(ev_fork, cs), "lookahead fork") ||
+                              check_cuda(cudaStreamWaitEvent(stream, ev_fork, 0),
+                                         "lookahead fork")))
+                    return RC_DEVICE_ERROR;
+                const size_t o = (size_t)W2 * kp;
+                rc = gemm_presplit_run(R2, R2, kp, Qh + o, Ql + o, Qh + o, Ql + o,
+                                       Cf + (size_t)(J + W + W2) * n + (J + W + W2), n, -1.0f,
+                                       1, gemm_err, stream);
+                if (rc) return rc;
+                if (ahead) {
+                    if (check_cuda(cudaEventRecord(ev_join, stream), "lookahead join"))
+                        return RC_DEVICE_ERROR;
+                    pending = true;
+                }
+            }
         }
     }
+    // the caller's stream continues after the chain's last work
+    if (ahead && (check_cuda(cudaEventRecord(ev_fork, cs), "lookahead end") ||
+                  check_cuda(cudaStreamWaitEvent(stream, ev_fork, 0), "lookahead end")))
+        return RC_DEVICE_ERROR;
     zero_upper_kernel<T><<<1024, 256, 0, stream>>>(A, n);
     note_launch();
     return check_cuda(cudaGetLastError(), "zero_upper launch") ? RC_DEVICE_ERROR : RC_OK;
@@ -585,8 +645,10 @@ dl_apply_kernel(const T* __restrict__ L, int n, const T* __restrict__ DLi,
 
 template <typename T>
 int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream_t stream,
-              float* panel_ws, int* gemm_err) {
-    int rc = cholesky_lower<T>(A, n, dstatus, stream, panel_ws, gemm_err);
+              float* panel_ws, int* gemm_err, cudaStream_t side, cudaEvent_t ev_fork,
+              cudaEvent_t ev_join) {
+    int rc = cholesky_lower<T>(A, n, dstatus, stream, panel_ws, gemm_err, side, ev_fork,
+                               ev_join);
     if (rc) return rc;
     dl_inverse_kernel<T><<<n / 16, 256, 0, stream>>>(A, n, dDLi, dD);
     dim3 g((n + 255) / 256, n / 16);
@@ -596,9 +658,9 @@ int block_ldl(T* A, int n, float* Lout, T* dD, T* dDLi, int* dstatus, cudaStream
 }
 
 template int block_ldl<float>(float*, int, float*, float*, float*, int*, cudaStream_t, float*,
-                              int*);
+                              int*, cudaStream_t, cudaEvent_t, cudaEvent_t);
 template int block_ldl<double>(double*, int, float*, double*, double*, int*, cudaStream_t,
-                               float*, int*);
+                               float*, int*, cudaStream_t, cudaEvent_t, cudaEvent_t);
 
 // ------------------------------------------------------------ quantize() U path
 // Ui = U^-1 for upper-triangular U (fp64), column by column (one thread per
