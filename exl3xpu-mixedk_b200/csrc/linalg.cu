@@ -117,40 +117,15 @@ __device__ __forceinline__ T dsqrt(T v);
 template <> __device__ __forceinline__ float dsqrt<float>(float v) { return sqrtf(v); }
 template <> __device__ __forceinline__ double dsqrt<double>(double v) { return sqrt(v); }
 
-// Inverse of the factored block in S (see potrf_diag_kernel), 1024 threads.
-__device__ __forceinline__ void potrf_inverse(const float (&S)[kNB][kNB + 1], int nb,
-                                              float* __restrict__ Linv, int t) {
-    using T = float;
-    __shared__ T X[kNB][kNB + 1];
-    const int c = t >> 4, q = t & 15;           // column, lane within its half-warp
-    for (int j = 0; j < kNB; ++j) {
-        const bool act = c < nb && j < nb && j >= c;
-        T part = T(0);
-        if (act)
-            for (int m = c + q; m < j; m += 16) part += S[j][m] * X[m][c];
-#pragma unroll
-        for (int off = 8; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off, 16);
-        if (q == 0) X[j][c] = act ? ((j == c) ? T(1) / S[j][j] : -part / S[j][j]) : T(0);
-        __syncwarp();
-    }
-    __syncthreads();
-    for (int idx = t; idx < kNB * kNB; idx += 1024) Linv[idx] = X[idx / kNB][idx % kNB];
-}
-
 // Factor the kNB x kNB diagonal block at (j0, j0) in place (lower).  1024
 // threads as 32 x 32; every thread derives the pivot's square root from
 // shared memory itself (the same value everywhere), so a column costs two
 // barriers: scale the column, then the rank-1 update of the trailing lower
-// triangle, 2-D strided without integer division.
-// Linv (optional, [kNB][kNB] row-major): also the inverse of the factored
-// block, lower triangular, zero above the diagonal (and outside nb x nb).
-// Column c of the inverse solves L x = e_c by forward substitution: 16
-// threads per column (one half-warp) split each step's sum and combine it
-// with shuffles, so the 64 steps need no block barrier.
+// triangle, 2-D strided without integer division.  (The fp64 and fp32-SIMT
+// path; the fp32 tensor-core path uses potrf_inv_kernel.)
 template <typename T>
 __global__ void __launch_bounds__(1024)
-potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ status,
-                  T* __restrict__ Linv = nullptr) {
+potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ status) {
     __shared__ T S[kNB][kNB + 1];
     if (*status) return;
     const int t = threadIdx.x;
@@ -178,9 +153,6 @@ potrf_diag_kernel(T* __restrict__ A, int n, int j0, int nb, int* __restrict__ st
     }
     for (int r = ty; r < nb; r += 32)
         for (int c = tx; c <= r; c += 32) A[(size_t)(j0 + r) * n + (j0 + c)] = S[r][c];
-    if constexpr (sizeof(T) == 4) {             // the fp32 tensor-core path only
-        if (Linv != nullptr) potrf_inverse(S, nb, Linv, t);
-    }
 }
 
 
