@@ -1,14 +1,16 @@
 // gemm_tc.cu -- LDLQ feedback-cache update on tcgen05 tensor cores, fed by TMA.
 //
-// Reference: quantize/quantize.py:742-744 -- after each 128-row buffer of the
+// Reference: quantize/quantize.py:742-744 -- after each buffer of the
 // right-to-left sweep,  prod += Lfac[16lo:16cur, :]^T @ (W - hatW)[16lo:16cur, :].
+// (The block LDL's trailing updates use the same kernels: linalg.cu.)
 // Only rows < 16lo of prod are ever read again, so the update is
 //   C[M][N] += A[M][K] . B[K][N],   M = 16 lo, N = n, K = 16 (cur - lo),
 // with A = Lfac[buf rows, :M]^T and B = E[buf rows, :] -- both stored with the
 // M / N index contiguous, C = prod row-major fp32.
 //
-// One CTA (128 threads) owns a 128 x 128 tile of C and walks K in 32-deep
-// chunks through a two-stage pipeline:
+// Two implementations.  The per-tile split kernel (feedback_gemm_tc_kernel,
+// used without split scratch): one CTA (128 threads) owns a 128 x 128 tile of
+// C and walks K in 32-deep chunks through a two-stage pipeline:
 //   * TMA loads 32 x 32 fp32 boxes of A and B (128-byte swizzle) into a staging
 //     buffer, while the previous chunk is being converted / multiplied.
 //   * Each thread takes one M (N) row of the chunk out of staging, splits every

@@ -10,7 +10,8 @@
 //   trellis int16 [k/16][n_seg/16][16K] per column segment (output)
 //
 // Sweep (host loop, all launches on one stream): k-blocks right to left in
-// 128-row buffers.  One tile-kernel launch per buffer covers all its k-blocks x
+// launch buffers of max(buf_cols, 512) rows.  One tile-kernel launch per
+// buffer covers all its k-blocks x
 // column tiles.  Launches with at least two tiles per SM use the persistent
 // lazy-argmin kernel (ldlq_lazy.cu); the others, one CTA per tile
 // with the traced encoder, below.  Each CTA takes a ticket in dependency order (k-block

@@ -1,16 +1,19 @@
-// linalg.cu -- Hessian factorisation for BlockLDLQ on fp32/fp64 CUDA cores.
+// linalg.cu -- Hessian factorisation for BlockLDLQ (fp32 with tensor-core
+// updates, fp64 on CUDA cores).
 //
 // Reference: quantize/quantize.py:419-437 block_LDL (Cholesky, 16x16 diagonal
 // block inverses, L <- L . blockdiag(DL^-1), identity diagonal blocks) with
 // the fp32 path of quantize_linear (:816) and the fp64 paths of its fallback
 // (:817-835) and of quantize()'s U -> G conversion (:944-950).
 //
-// Cholesky: blocked right-looking, panel 64: (1) one CTA factors the 64x64
-// diagonal block in shared memory and records a LAPACK-style info (1-based
-// column of the first non-positive / non-finite pivot) in a device status
-// word; (2) rows below solve against the panel (triangular solve); (3) SIMT
-// GEMM updates the trailing lower triangle.  Later launches skip work once the
-// status is set; the host reads the status once at the end.
+// Cholesky: blocked right-looking, 64-column steps: (1) one CTA factors the
+// 64x64 diagonal block in shared memory and records a LAPACK-style info
+// (1-based column of the first non-positive / non-finite pivot) in a device
+// status word; (2) rows below solve against it; (3) the trailing lower
+// triangle is updated -- fp32: on tcgen05 tensor cores (gemm_tc.cu) in two
+// levels of blocking with a lookahead stream (cholesky_lower); fp64: SIMT
+// GEMM.  Later launches skip work once the status is set; the host reads the
+// status once at the end.
 #include "exl3b_internal.h"
 
 namespace exl3b {

@@ -301,9 +301,9 @@ __device__ __forceinline__ void vit_load_bin(const float* __restrict__ Bc, int m
 // One trellis step: best_{i+1} = min-plus over this thread's states using
 // best_i (Bc) and target x; writes best_{i+1} (Bn), returns packed argmins
 // (output e's argmin w in bits [e*BPE, e*BPE + BPE)); 0 when !TRACK.
-// grow (untraced steps of the slice geometries, K >= 4): also store this
-// thread's outputs to a global row in natural index order -- contiguous NJ
-// floats per thread, one or two vector stores.
+// grow (untraced steps of the slice geometries, K >= 4; the lazy pass uses it
+// at K >= 5): also store this thread's outputs to a global row in natural
+// index order -- contiguous NJ floats per thread, one or two vector stores.
 template <int K, bool TRACK = true>
 __device__ __forceinline__ uint64_t vit_step(const __half2 (&f2)[64], float x,
                                              const float* __restrict__ Bc,
