@@ -23,8 +23,10 @@ The default line is configuration 2 (the driver's bench line).  --config c3
 (fused q/k/v module, K = [5, 7, 7], one shared Hessian) and --config c4
 (17408 -> 5120 down projection at --K) print the same line for those
 workloads.  "kernels" adds each device stage's roofline: the fused tile kernel
-(ALU lanes), the tcgen05 feedback GEMM (useful FLOP vs the TF32 tensor rate),
-the Hadamard rotations (HBM bytes) and the block LDL (fp32 FMA rate).
+(fp32 lanes: 3 rounded fp32 ops per add-compare-select), the tcgen05 feedback
+GEMM (useful FLOP vs the TF32 tensor rate), the Hadamard rotations (HBM bytes)
+and the block LDL (k^3/3 FLOP against the fp32 FMA rate, although its trailing
+updates run on the tensor cores).
 
 --impl reference times the reference algorithm's CPU implementation (the C/numpy
 restatement under oracle/; the reference itself is Python and does not travel)
