@@ -202,6 +202,23 @@ size_t exl3b_block_ldl_workspace_bytes(int k, int f64) {
            (f64 ? 0 : align256(ldl_panel_bytes(k)) + 256);
 }
 
+// The device's high-priority helper stream and its fork / join events,
+// created on first use (the block LDL's lookahead, the sweep's concurrent
+// segment launches).
+static int side_stream(DeviceState* st) {
+    if (st->side) return RC_OK;
+    int lo_pri = 0, hi_pri = 0;
+    cudaDeviceGetStreamPriorityRange(&lo_pri, &hi_pri);
+    if (check_cuda(cudaStreamCreateWithPriority(&st->side, cudaStreamNonBlocking, hi_pri),
+                   "helper stream") ||
+        check_cuda(cudaEventCreateWithFlags(&st->ev_fork, cudaEventDisableTiming),
+                   "helper event") ||
+        check_cuda(cudaEventCreateWithFlags(&st->ev_join, cudaEventDisableTiming),
+                   "helper event"))
+        return RC_DEVICE_ERROR;
+    return RC_OK;
+}
+
 int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
                     size_t ws_bytes, void* stream) {
     if (k <= 0 || k % 16) { set_error("k=%d must be a positive multiple of 16", k); return RC_BAD_REQUEST; }
@@ -226,18 +243,8 @@ int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
     if (check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "memset status") ||
         (gerr && check_cuda(cudaMemsetAsync(gerr, 0, sizeof(int), s), "memset gemm status")))
         return RC_DEVICE_ERROR;
-    // the lookahead's helper stream and events (per device, created once)
-    if (!f64 && !st->side) {
-        int lo_pri = 0, hi_pri = 0;
-        cudaDeviceGetStreamPriorityRange(&lo_pri, &hi_pri);
-        if (check_cuda(cudaStreamCreateWithPriority(&st->side, cudaStreamNonBlocking, hi_pri),
-                       "lookahead stream") ||
-            check_cuda(cudaEventCreateWithFlags(&st->ev_fork, cudaEventDisableTiming),
-                       "lookahead event") ||
-            check_cuda(cudaEventCreateWithFlags(&st->ev_join, cudaEventDisableTiming),
-                       "lookahead event"))
-            return RC_DEVICE_ERROR;
-    }
+    // the lookahead's helper stream and events
+    if (!f64 && side_stream(st)) return RC_DEVICE_ERROR;
     prof_begin_launch(s, PROF_LDL, (double)k * k * k / 3.0);
     int rc = f64 ? block_ldl<double>(static_cast<double*>(dA), k, dLfac, static_cast<double*>(dD),
                                      static_cast<double*>(dli), status, s)
@@ -383,7 +390,14 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     a.slots = ctrl;
     a.colprog = ctrl + a.nslots;
     a.tickets = a.colprog + tn;
-    a.err = a.tickets + 1;
+    a.err = a.tickets + 1;                 // err[0..4]
+    a.tickets2 = a.tickets + 8;
+    if (nseg > 1) {                        // segments of different K can run side by side
+        if (side_stream(st)) return RC_DEVICE_ERROR;
+        a.side = st->side;
+        a.ev_fork = st->ev_fork;
+        a.ev_join = st->ev_join;
+    }
     a.Wq = dWq; a.Lfac = dLfac; a.k = k; a.n = n;
     a.nseg = nseg; a.seg_c0 = seg_c0; a.seg_K = seg_K; a.seg_trellis = seg_trellis;
     a.pivot = pivot; a.margin = margin; a.buf_cols = buf_cols;

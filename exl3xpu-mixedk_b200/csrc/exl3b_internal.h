@@ -162,6 +162,9 @@ struct SweepArgs {
     float* lazy_ws;          // lazy pipeline: SMs x 2 row regions (lazy_pipeline launches)
     void* split_ws;          // feedback GEMM pre-split operands (null: per-tile split)
     size_t split_bytes;
+    int* tickets2;           // ticket counter of launches on the helper stream
+    cudaStream_t side;       // helper stream (null: every launch on the caller's)
+    cudaEvent_t ev_fork, ev_join;
     int nslots;              // backpointer slots (> SM count)
     int* slots;              // [nslots] ownership flags (zero at sweep start)
     int* colprog;            // [tn] finished k-blocks per column (zero at start)

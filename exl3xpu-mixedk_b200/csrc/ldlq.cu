@@ -224,35 +224,80 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
 
     // k-blocks [lo, hi) of buffer end `cur`: one launch per distinct K over the
     // column segments of that K
+    int kmin = 8;
+    for (int s = 0; s < a.nseg; ++s) kmin = a.seg_K[s] < kmin ? a.seg_K[s] : kmin;
     auto launch = [&](int cur, int lo, int hi) -> int {
         p.cur = cur;
         p.top = hi - 1;
-        p.tickets = a.tickets;
+        struct Group { int K, nls; int ls_seg[kMaxSeg]; int ls_pre[kMaxSeg + 1]; long long nb; };
+        Group g[kMaxSeg];
+        int ng = 0, big = 0;
+        long long total = 0;
         bool done[kMaxSeg] = {};
         for (int s0 = 0; s0 < a.nseg; ++s0) {
             if (done[s0]) continue;
-            const int K = a.seg_K[s0];
-            p.nls = 0;
-            p.ls_pre[0] = 0;
+            Group& G = g[ng];
+            G.K = a.seg_K[s0];
+            G.nls = 0;
+            G.ls_pre[0] = 0;
             for (int s1 = s0; s1 < a.nseg; ++s1) {
-                if (a.seg_K[s1] != K) continue;
+                if (a.seg_K[s1] != G.K) continue;
                 done[s1] = true;
-                p.ls_seg[p.nls] = s1;
-                p.ls_pre[p.nls + 1] = p.ls_pre[p.nls] + (a.seg_c0[s1 + 1] - a.seg_c0[s1]);
-                ++p.nls;
+                G.ls_seg[G.nls] = s1;
+                G.ls_pre[G.nls + 1] = G.ls_pre[G.nls] + (a.seg_c0[s1 + 1] - a.seg_c0[s1]);
+                ++G.nls;
             }
-            if (check_cuda(cudaMemsetAsync(a.tickets, 0, sizeof(int), stream), "memset tickets"))
+            G.nb = (long long)(hi - lo) * G.ls_pre[G.nls];
+            total += G.nb;
+            if (G.nb > g[big].nb) big = ng;
+            ++ng;
+        }
+        // Segments of different K side by side: columns never interact, so the
+        // largest group runs on the caller's stream with its share of the SMs
+        // and the others, one after another, on the helper stream with the
+        // rest (own ticket counter, row regions after the first share's).  A
+        // narrow segment alone on the whole GPU would leave its CTAs waiting
+        // for the block below in their column.  Only when every launch keeps
+        // at least two tiles per CTA (the lazy pipeline); else one after
+        // another on the caller's stream, each over all SMs.
+        int grid_big = sms, grid_side = 0;
+        bool conc = false;
+        if (ng > 1 && a.side && a.lazy_ws && sms > 1) {
+            grid_big = (int)((double)sms * (double)g[big].nb / (double)total + 0.5);
+            grid_big = grid_big < 1 ? 1 : (grid_big > sms - 1 ? sms - 1 : grid_big);
+            grid_side = sms - grid_big;
+            conc = lazy_pipeline(g[big].K, g[big].nb, grid_big);
+            for (int i = 0; i < ng; ++i)
+                if (i != big) conc = conc && lazy_pipeline(g[i].K, g[i].nb, grid_side);
+        }
+        if (conc && (check_cuda(cudaEventRecord(a.ev_fork, stream), "segment fork") ||
+                     check_cuda(cudaStreamWaitEvent(a.side, a.ev_fork, 0), "segment fork")))
+            return RC_DEVICE_ERROR;
+        for (int i = 0; i < ng; ++i) {
+            const Group& G = g[i];
+            const bool on_side = conc && i != big;
+            cudaStream_t s = on_side ? a.side : stream;
+            p.nls = G.nls;
+            for (int m = 0; m < G.nls; ++m) p.ls_seg[m] = G.ls_seg[m];
+            for (int m = 0; m <= G.nls; ++m) p.ls_pre[m] = G.ls_pre[m];
+            p.tickets = on_side ? a.tickets2 : a.tickets;
+            p.lazy_ws = on_side ? a.lazy_ws + (size_t)grid_big * 2 * (lazy_region_bytes(kmin) / 4)
+                                : a.lazy_ws;
+            if (check_cuda(cudaMemsetAsync(p.tickets, 0, sizeof(int), s), "memset tickets"))
                 return RC_DEVICE_ERROR;
-            const long long nb = (long long)(hi - lo) * p.ls_pre[p.nls];
-            p.ntiles = (int)nb;
-            prof_begin_launch(stream, PROF_TILE, (double)nb * 256.0);
+            p.ntiles = (int)G.nb;
+            const int grid = conc ? (on_side ? grid_side : grid_big) : sms;
+            prof_begin_launch(s, PROF_TILE, (double)G.nb * 256.0);
             // at least two tiles per SM: persistent CTAs, lazy argmin
-            const bool lazy = a.lazy_ws != nullptr && lazy_pipeline(K, nb, sms);
-            const int rc = lazy ? launch_lazy_tile(K, p, (unsigned)sms, stream)
-                                : launch_tile(K, p, (unsigned)nb, stream);
-            prof_end_launch(stream);
+            const bool lazy = a.lazy_ws != nullptr && lazy_pipeline(G.K, G.nb, grid);
+            const int rc = lazy ? launch_lazy_tile(G.K, p, (unsigned)grid, s)
+                                : launch_tile(G.K, p, (unsigned)G.nb, s);
+            prof_end_launch(s);
             if (rc) return rc;
         }
+        if (conc && (check_cuda(cudaEventRecord(a.ev_join, a.side), "segment join") ||
+                     check_cuda(cudaStreamWaitEvent(stream, a.ev_join, 0), "segment join")))
+            return RC_DEVICE_ERROR;
         return RC_OK;
     };
     if (!a.Lfac) {
