@@ -270,6 +270,9 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
             for (int i = 0; i < ng; ++i)
                 if (i != big) conc = conc && lazy_pipeline(g[i].K, g[i].nb, grid_side);
         }
+        // profiling: a concurrent group is one interval on the caller's stream
+        // (fork to join) doing all its tiles
+        if (conc) prof_begin_launch(stream, PROF_TILE, (double)total * 256.0);
         if (conc && (check_cuda(cudaEventRecord(a.ev_fork, stream), "segment fork") ||
                      check_cuda(cudaStreamWaitEvent(a.side, a.ev_fork, 0), "segment fork")))
             return RC_DEVICE_ERROR;
@@ -287,17 +290,18 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
                 return RC_DEVICE_ERROR;
             p.ntiles = (int)G.nb;
             const int grid = conc ? (on_side ? grid_side : grid_big) : sms;
-            prof_begin_launch(s, PROF_TILE, (double)G.nb * 256.0);
+            if (!conc) prof_begin_launch(s, PROF_TILE, (double)G.nb * 256.0);
             // at least two tiles per SM: persistent CTAs, lazy argmin
             const bool lazy = a.lazy_ws != nullptr && lazy_pipeline(G.K, G.nb, grid);
             const int rc = lazy ? launch_lazy_tile(G.K, p, (unsigned)grid, s)
                                 : launch_tile(G.K, p, (unsigned)G.nb, s);
-            prof_end_launch(s);
+            if (!conc) prof_end_launch(s);
             if (rc) return rc;
         }
         if (conc && (check_cuda(cudaEventRecord(a.ev_join, a.side), "segment join") ||
                      check_cuda(cudaStreamWaitEvent(stream, a.ev_join, 0), "segment join")))
             return RC_DEVICE_ERROR;
+        if (conc) prof_end_launch(stream);
         return RC_OK;
     };
     if (!a.Lfac) {
