@@ -252,7 +252,13 @@ int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
                                     static_cast<float*>(dli), status, s, panel, gerr, st->side,
                                     st->ev_fork, st->ev_join);
     prof_end_launch(s);
-    if (rc) return rc;
+    if (rc) {
+        // the lookahead chain may still run on the helper stream: let it end
+        // before the caller can release the workspace
+        if (!f64 && st->side) cudaStreamSynchronize(st->side);
+        cudaStreamSynchronize(s);
+        return rc;
+    }
     int h = 0, g = 0;
     if (check_cuda(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, s),
                    "read status") ||
@@ -411,7 +417,13 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
             return RC_DEVICE_ERROR;
     }
     int rc = ldlq_sweep(a, s);
-    if (rc) return rc;
+    if (rc) {
+        // work may still run on the helper stream: nothing of the workspace
+        // may be released before it ends
+        if (a.side) cudaStreamSynchronize(a.side);
+        cudaStreamSynchronize(s);
+        return rc;
+    }
     // the tile kernels bound every dependency wait; report a time-out
     int err[14] = {};
     if (check_cuda(cudaMemcpyAsync(err, a.err, sizeof(err), cudaMemcpyDeviceToHost, s),
