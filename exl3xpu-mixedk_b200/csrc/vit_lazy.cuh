@@ -17,9 +17,9 @@
 //      shared-memory writes to the copy engine is paid once per batch.
 //    - K >= 5 (rows of 8 KB and less): each thread stores its outputs of the
 //      step to the row itself (natural index order, one or two vector
-//      stores), which measured faster there than the copy engine.  The end state of a pass (the first-index argmin over the last
-//    step's costs) is found by rescanning only the group(s) that reach the
-//    minimum.
+//      stores), which measured faster there than the copy engine.
+//    The end state of a pass (the first-index argmin over the last step's
+//    costs) is found by rescanning only the group(s) that reach the minimum.
 //  * The traceback recomputes, for the one group j = s >> K on the path, the
 //    2^K candidate costs cost_{r-1}(j + w 2^(16-K)) = fl(fl(f - x)^2) + best_{r-1}
 //    from the stored row with the same fp32 operations as the forward step,
@@ -31,10 +31,10 @@
 //    barrier of their own, so the job warp never waits for them nor they for
 //    it: it reads only completed rows of its own tile, and its serial latency
 //    (fetch, cost, warp reduction per row) stays off the forward critical
-//    path.  The two meet again at the end of the pass.  A CTA
-//    therefore keeps two tiles in
-//    flight and runs them in four phases per pair (F = forward pass, T =
-//    traceback; pass 2 needs pass 1's traceback, the write-back needs pass 2's):
+//    path.  The two meet again at the end of the pass.  A CTA therefore keeps
+//    two tiles in flight and runs them in four phases per pair (F = forward
+//    pass, T = traceback; pass 2 needs pass 1's traceback, the write-back
+//    needs pass 2's):
 //        F1(A) | T2(previous B)
 //        F1(B) | T1(A)
 //        F2(A) | T1(B)
