@@ -38,7 +38,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import subprocess
 import sys
 import threading
@@ -54,15 +53,26 @@ METRIC = "trellis-encoded weights/s (Viterbi+LDLQ) at K=4"
 UNIT = "weights/s"
 K_BITS = 4
 DIM = 5120
-# Per weight (one trellis step per weight and pass, 2 passes at margin 0):
-# 2 x 2^16 add-compare-selects, each 3 correctly rounded fp32 operations
-# (f - x, its square, + best: fusing any two would change the rounding); the
-# minimum runs on the ALU pipe beside them.  The fp32 pipe retires 128 lane
-# operations per SM per clock (the packed f32x2 forms issue at half rate, so
-# they save issue slots but not fp32 throughput).
-OPS_PER_WEIGHT = 2 * 65536 * 3
-FP32_NOTE = ("3 rounded fp32 ops (sub, square, add) per add-compare-select; "
-             "the min runs on the ALU pipe")
+# Algorithmic work per weight (one trellis step per weight and pass, 2 passes
+# at margin 0): 2 x 2^16 add-compare-selects, counted as 2 fp32 lane ops each
+# (the add and the compare-select): 262144 ops per weight.  This is the
+# roofline's `achieved`.  Bit-exactness with the reference's fp32 "sq" emit
+# needs 3 correctly rounded fp32 operations per add-compare-select (f - x,
+# its square, + best; fusing any two changes the rounding) with the minimum on
+# the ALU pipe beside them: that fp32-pipe floor is reported as a second
+# fraction.  The fp32 pipe retires 128 lane operations per SM per clock (the
+# packed f32x2 forms issue at half rate: they save issue slots, not fp32
+# throughput).
+OPS_PER_WEIGHT = 2 * 65536 * 2
+FLOOR_OPS_PER_WEIGHT = 2 * 65536 * 3
+FP32_NOTE = ("2 ops (add, compare-select) per add-compare-select, 2 x 2^16 per weight; "
+             "peak = SMs x 128 fp32 lanes x max SM clock")
+# DRAM traffic of the tile kernel per encoded weight, K = 4: dram__bytes_read.sum +
+# dram__bytes_write.sum of one ldlq_lazy_kernel<4> launch of the 2048 x 2048
+# profiling case (4096 tiles, 1048576 weights), divided by its weights; the bench
+# scales it to a full launch (traffic grows with the tiles: rows per tile are
+# fixed).  Mostly the lazy-argmin rows (2^(18-K) bytes per traced step).
+TRAFFIC_BYTES_PER_WEIGHT_K4 = 26822
 WORKLOAD = ("config 2: single dense projection 5120x5120 bf16 ~N(0,0.02^2) + 0.1% x10 "
             "outliers; H = A^T A/4096, A Student-t(4) x lognormal(1) channel scales; "
             "random-sign Hadamard, damped block-LDL, full BlockLDLQ + tail-biting "
@@ -82,19 +92,6 @@ def _measured_peaks():
             return json.load(f)
     except OSError:
         return {}
-
-
-def _profile_traffic():
-    """DRAM bytes per encoded weight of the tile kernel from the committed ncu
-    summary (line 'traffic_bytes_per_weight: N'), or None; scaled by the
-    weights one launch encodes."""
-    p = os.path.join(REPO, "profiles", "ldlq_tile_kernel_c2.md")
-    try:
-        txt = open(p).read()
-    except OSError:
-        return None
-    m = re.search(r"traffic_bytes_per_weight:\s*([0-9.eE+]+)", txt)
-    return float(m.group(1)) if m else None
 
 
 class ClockSampler:
@@ -435,7 +432,8 @@ def main():
     tile_ms_avg = ms_tile / max(n_tile, 1)
     w_per_launch = u_tile / max(n_tile, 1)
     achieved = w_per_launch * OPS_PER_WEIGHT / (tile_ms_avg / 1e3) / 1e9
-    tpw = _profile_traffic()
+    floor_achieved = w_per_launch * FLOOR_OPS_PER_WEIGHT / (tile_ms_avg / 1e3) / 1e9
+    tpw = TRAFFIC_BYTES_PER_WEIGHT_K4 if shape.get("K") == 4 else None
     roofline = {
         "kernel": "LDLQ tile kernel (fused feedback + tail-biting Viterbi + write-back; "
                   "ldlq_lazy_kernel for launches of >= 2 tiles per SM)",
@@ -444,11 +442,18 @@ def main():
         "peak_source": f"{sms} SMs x 128 fp32 lanes x {mhz:.0f} MHz (sm_max_mhz of "
                        f"MEASURED_PEAKS.json); {FP32_NOTE}",
         "ops_per_weight": OPS_PER_WEIGHT,
+        "frac_fp32_floor": floor_achieved / peak_ops,
+        "fp32_floor_note": "3 correctly rounded fp32 ops per add-compare-select "
+                           "(393216 per weight), the least a bit-exact encoder executes",
         "launches_per_step": n_tile / args.steps,
         "avg_launch_ms": tile_ms_avg,
         "share_of_step": ms_tile / args.steps / ms if ms else None,
         "traffic": (tpw * w_per_launch) if tpw else None,
-        "traffic_unit": "bytes per launch",
+        "traffic_unit": "bytes per launch (ncu DRAM bytes per weight of the 2048^2 "
+                        "profiling launch x weights per launch)",
+        "algorithmic_bytes_per_launch": w_per_launch * 2 * 2 ** (16 - shape["K"]) *
+                                        shape["K"] / 8 if isinstance(shape.get("K"), int)
+                                        else None,
     }
 
     in_bytes = _nbytes(inputs)

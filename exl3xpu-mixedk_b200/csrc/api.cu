@@ -35,6 +35,11 @@ int check_cuda(cudaError_t e, const char* what) {
     return 1;
 }
 
+// ---------------------------------------------------------------- wait bound
+// Bound of the LDLQ sweep's device-side waits (ns); exl3b_set_wait_limit_ms.
+static std::atomic<double> g_wait_ns{4.0e9};
+double sweep_wait_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
+
 // ---------------------------------------------------------------- accounting
 static std::atomic<long long> g_launches{0};
 void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
@@ -219,6 +224,15 @@ int exl3b_profile_end(int kind, double* ms_total, long long* launches, double* u
 
 int exl3b_abi_version(void) { return EXL3B_ABI_VERSION; }
 
+int exl3b_set_wait_limit_ms(double ms) {
+    if (!(ms >= 0.0) || ms > 60000.0) {
+        set_error("wait limit %g ms outside [0, 60000]", ms);
+        return RC_BAD_REQUEST;
+    }
+    g_wait_ns.store(ms == 0.0 ? 4.0e9 : ms * 1.0e6);
+    return RC_OK;
+}
+
 int exl3b_code_lut(int code, float* out65536) { return build_code_lut(code, out65536); }
 
 int exl3b_device_init(int device) {
@@ -278,6 +292,50 @@ int exl3b_tailbite(const float* dX, int nseq, int K, int code, int pivot,
     if (rc) return rc;
     return launch_tailbite(dX, nseq, K, pivot, margin, dStates, ws, plan, tab,
                            st->lut32[code], static_cast<cudaStream_t>(stream));
+}
+
+size_t exl3b_viterbi_workspace_bytes(int nseq, int K) {
+    if (K < 2 || K > 7 || nseq <= 0) return 0;
+    const int sms = device_sms();
+    const int grid = nseq < sms ? nseq : sms;
+    return (size_t)grid * bp_slot_bytes(K);
+}
+
+int exl3b_viterbi(const float* dX, int nseq, int T, int K, int code,
+                  const int32_t* dOverlap, int back_from, int32_t* dStates,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+    if (K < 2 || K > 7) { set_error("K=%d outside 2..7", K); return RC_BAD_K; }
+    if (nseq <= 0) { set_error("nseq=%d", nseq); return RC_BAD_NSEQ; }
+    if (T < 1 || T > kSteps) {
+        set_error("T=%d: a pass covers 1..%d steps", T, kSteps);
+        return RC_BAD_REQUEST;
+    }
+    if (code < 0 || code > 2) { set_error("code id %d", code); return RC_BAD_REQUEST; }
+    if (back_from < -1) { set_error("back_from=%d (-1 = none)", back_from); return RC_BAD_REQUEST; }
+    if (!dX || !dStates) { set_error("X and states must be device pointers"); return RC_BAD_REQUEST; }
+    DeviceState* st = nullptr;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    const int grid = nseq < st->sms ? nseq : st->sms;
+    const size_t need = (size_t)grid * bp_slot_bytes(K);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if (ws) {
+        if (workspace_bytes < need || ((uintptr_t)ws & 255)) {
+            set_error("workspace %zu bytes < %zu or not 256-byte aligned",
+                      workspace_bytes, need);
+            return RC_WORKSPACE;
+        }
+    } else {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = grow(&st->scratch, &st->scratch_bytes, need);
+        if (rc) return rc;
+        ws = st->scratch;
+    }
+    const uint4* tab = nullptr;
+    rc = f2tab_get(st, code, K, &tab);
+    if (rc) return rc;
+    return launch_viterbi(dX, nseq, T, K, dOverlap, back_from, dStates, ws, grid, tab,
+                          static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------------------------

@@ -202,6 +202,27 @@ size_t exl3b_block_ldl_workspace_bytes(int k, int f64) {
            (f64 ? 0 : align256(ldl_panel_bytes(k)) + 256);
 }
 
+// After a failed launch sequence that may have forked work onto the helper
+// stream: outside a stream capture, wait until both streams are idle (the
+// caller may release the workspace once the call returns); inside a capture,
+// where synchronising is not allowed and would invalidate it, join the helper
+// stream back into the caller's with the join event instead.  The results of
+// these calls are deliberately not checked: the error already recorded is the
+// one reported.
+static void drain_after_error(cudaStream_t s, DeviceState* st, bool side_used) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusNone;
+    if (cs != cudaStreamCaptureStatusNone) {
+        if (side_used && st->side && st->ev_join) {
+            (void)cudaEventRecord(st->ev_join, st->side);
+            (void)cudaStreamWaitEvent(s, st->ev_join, 0);
+        }
+        return;
+    }
+    if (side_used && st->side) (void)cudaStreamSynchronize(st->side);
+    (void)cudaStreamSynchronize(s);
+}
+
 // The device's high-priority helper stream and its fork / join events,
 // created on first use (the block LDL's lookahead, the sweep's concurrent
 // segment launches).
@@ -255,8 +276,7 @@ int exl3b_block_ldl(void* dA, int k, int f64, float* dLfac, void* dD, void* ws,
     if (rc) {
         // the lookahead chain may still run on the helper stream: let it end
         // before the caller can release the workspace
-        if (!f64 && st->side) cudaStreamSynchronize(st->side);
-        cudaStreamSynchronize(s);
+        drain_after_error(s, st, !f64);
         return rc;
     }
     int h = 0, g = 0;
@@ -410,6 +430,7 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     a.hatW = dHatW; a.states = dStates; a.xout = dXout;
     a.f2tab = tabs; a.lut32 = st->lut32[code];
     a.block_lo = block_lo; a.block_hi = block_hi;
+    a.wait_ns = sweep_wait_ns();
     cudaStream_t s = S(stream);
     if (block_hi == tk) {   // start of a sweep: feedback cache and control words
         if ((dLfac && check_cuda(cudaMemsetAsync(a.prod, 0, (size_t)k * n * 4, s), "memset prod")) ||
@@ -420,8 +441,7 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
     if (rc) {
         // work may still run on the helper stream: nothing of the workspace
         // may be released before it ends
-        if (a.side) cudaStreamSynchronize(a.side);
-        cudaStreamSynchronize(s);
+        drain_after_error(s, st, a.side != nullptr);
         return rc;
     }
     // the tile kernels bound every dependency wait; report a time-out
@@ -482,6 +502,30 @@ int exl3b_feedback_gemm(int M, int N, int K, const float* dA_T, int lda, const f
         return RC_DEVICE_ERROR;
     }
     return RC_OK;
+}
+
+int exl3b_verify_trellis(const int16_t* dTrellis, int tk, int tn, int K, int code,
+                         const float* dHatW, int ldw, const int32_t* dStates, int ld_states,
+                         int* dMismatch, void* stream) {
+    if (K < 2 || K > 7) { set_error("K=%d", K); return RC_BAD_K; }
+    if (code < 0 || code > 2 || tk < 0 || tn < 0 || ldw < 16 * tn ||
+        (dStates && ld_states < tn) || !dTrellis || !dHatW || !dMismatch) {
+        set_error("verify: code %d, [%d x %d] tiles, ldw %d, ld_states %d", code, tk, tn,
+                  ldw, ld_states);
+        return RC_BAD_REQUEST;
+    }
+    DeviceState* st;
+    if (need_device(&st)) return RC_NO_DEVICE;
+    return launch_verify(dTrellis, tk, tn, K, st->lut32[code], dHatW, ldw, dStates, ld_states,
+                         dMismatch, S(stream));
+}
+
+int exl3b_hadamard_axis(const float* dX, int rows, int cols, int axis, float* dY,
+                        void* stream) {
+    if (!dX || !dY) { set_error("null matrix"); return RC_BAD_REQUEST; }
+    DeviceState* st;
+    if (need_device(&st)) return RC_NO_DEVICE;
+    return launch_had_axis(dX, rows, cols, axis, dY, S(stream));
 }
 
 int exl3b_pack_states(const int32_t* dStates, int ntiles, int K, int16_t* dOut, void* stream) {

@@ -68,6 +68,13 @@ size_t lazy_region_bytes(int K);
 int launch_tailbite(const float* dX, int nseq, int K, int pivot, int margin,
                     int32_t* dStates, uint8_t* ws, const TailbitePlan& plan,
                     const uint4* f2tab, const float* lut32, cudaStream_t stream);
+// Single Viterbi pass over nseq sequences of T <= 256 targets (X [nseq][T]):
+// optional per-sequence overlap pin, back_from < 0 for all states
+// ([nseq][T]) else the state at back_from ([nseq]).  Waves of `grid` CTAs,
+// one backpointer slot (bp_slot_bytes(K)) per CTA of a wave.
+int launch_viterbi(const float* dX, int nseq, int T, int K, const int32_t* dOverlap,
+                   int back_from, int32_t* dStates, uint8_t* ws, int grid,
+                   const uint4* f2tab, cudaStream_t stream);
 
 // ------------------------------------------------------------ incoherence
 struct HadParams {
@@ -170,6 +177,7 @@ struct SweepArgs {
     int* colprog;            // [tn] finished k-blocks per column (zero at start)
     int* tickets;            // launch ticket counter (zeroed before each launch)
     int* err;                // error word (zero at sweep start)
+    double wait_ns;          // bound of every device-side wait of the sweep
     const uint4* const* f2tab;  // [8] per K
     const float* lut32;
     int block_hi, block_lo;  // sweep blocks [block_lo, block_hi)
@@ -180,5 +188,18 @@ int launch_pack(const int32_t* st, int nt, int K, int16_t* out, cudaStream_t str
 int launch_unpack(const int16_t* tr, int nt, int K, int32_t* st, cudaStream_t stream);
 int launch_decode(const int16_t* tr, int tk, int tn, int K, const float* lut, float* W,
                   cudaStream_t stream);
+// Self-check of an encoded column segment (quantize.py:849-853, :958-963):
+// adds to *bad the number of weights whose value decoded from the trellis
+// [tk][tn][16K] differs from hatW (row pitch ldw floats) and, with states
+// (row pitch ld_states tiles of 256), of states unpacked from the trellis
+// that differ from the encoder's.
+int launch_verify(const int16_t* tr, int tk, int tn, int K, const float* lut,
+                  const float* hatW, int ldw, const int32_t* states, int ld_states, int* bad,
+                  cudaStream_t stream);
+// Wait bound (ns) of the sweep's device-side waits (exl3b_set_wait_limit_ms).
+double sweep_wait_ns();
+// One-sided block-128 Hadamard (had_left axis 0, had_right axis 1).
+int launch_had_axis(const float* X, int rows, int cols, int axis, float* Y,
+                    cudaStream_t stream);
 
 }  // namespace exl3b

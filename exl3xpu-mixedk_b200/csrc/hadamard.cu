@@ -184,6 +184,72 @@ int launch_had2(const HadParams& p, cudaStream_t stream) {
     return check_cuda(cudaGetLastError(), "had2_kernel launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
+// ------------------------------------------------------------ one-sided
+// had_left / had_right (quantize.py:135-146): the block-128 Hadamard along one
+// axis of X [rows][cols] only, so the other axis needs no multiple of 128.
+// fl32(1/sqrt(128)) is applied once after the butterflies (the reference's
+// fp32 GEMM with the normalised matrix rounds differently: agreement to fp32
+// rounding, like the two-sided transforms).
+constexpr float kInvSqrt128 = 0.08838834764831845f;
+
+// along the last axis: one warp per contiguous 128-vector, 4 values per lane
+__global__ void __launch_bounds__(256)
+had_last_kernel(const float* __restrict__ X, float* __restrict__ Y, size_t nvec) {
+    const size_t v = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (v >= nvec) return;
+    const float* x = X + v * kHB;
+    float a[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) a[q] = x[lane + 32 * q];
+    fwht128(a, lane);
+    float* y = Y + v * kHB;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) y[lane + 32 * q] = a[q] * kInvSqrt128;
+}
+
+// along the first axis: a CTA stages a 128-row x 32-column tile (coalesced
+// along the columns), each of its 8 warps transforms 4 columns
+__global__ void __launch_bounds__(256)
+had_first_kernel(const float* __restrict__ X, float* __restrict__ Y, int cols) {
+    __shared__ float tile[kHB][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * kHB;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = c0 + lane;
+    for (int r = warp; r < kHB; r += 8)
+        tile[r][lane] = c < cols ? X[(size_t)(r0 + r) * cols + c] : 0.0f;
+    __syncthreads();
+    for (int j = warp; j < 32; j += 8) {
+        float a[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) a[q] = tile[lane + 32 * q][j];
+        fwht128(a, lane);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tile[lane + 32 * q][j] = a[q] * kInvSqrt128;
+    }
+    __syncthreads();
+    if (c < cols)
+        for (int r = warp; r < kHB; r += 8) Y[(size_t)(r0 + r) * cols + c] = tile[r][lane];
+}
+
+int launch_had_axis(const float* X, int rows, int cols, int axis, float* Y,
+                    cudaStream_t stream) {
+    if (rows <= 0 || cols <= 0 || (axis == 0 ? rows : cols) % kHB || axis < 0 || axis > 1) {
+        set_error("Hadamard along axis %d of [%d, %d]: that dim must be a positive "
+                  "multiple of 128", axis, rows, cols);
+        return RC_BAD_REQUEST;
+    }
+    if (axis == 1) {
+        const size_t nvec = (size_t)rows * (cols / kHB);
+        had_last_kernel<<<(unsigned)((nvec * 32 + 255) / 256), 256, 0, stream>>>(X, Y, nvec);
+    } else {
+        dim3 grid((cols + 31) / 32, rows / kHB);
+        had_first_kernel<<<grid, 256, 0, stream>>>(X, Y, cols);
+    }
+    note_launch();
+    return check_cuda(cudaGetLastError(), "one-sided Hadamard launch") ? RC_DEVICE_ERROR : RC_OK;
+}
+
 // ------------------------------------------------------------ channel scales
 // EXL3 per-channel magnitude folds (quantize.py:785-800, 854-862, 1025-1041).
 

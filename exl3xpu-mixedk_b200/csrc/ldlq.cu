@@ -94,7 +94,7 @@ ldlq_tile_kernel(const __grid_constant__ LdlqTileParams p) {
             const unsigned h = (unsigned)ticket * 2654435761u;
             const int start = (int)(h % (unsigned)p.nslots);
             const long long t0 = clock64();
-            const long long limit = (long long)(kWaitNs * 2.0);
+            const long long limit = p.wait_cycles;
             while (slot < 0) {
                 for (int k = 0; k < p.nslots && slot < 0; ++k) {
                     int cand = start + k;
@@ -113,7 +113,7 @@ ldlq_tile_kernel(const __grid_constant__ LdlqTileParams p) {
         if (ok && p.Lfac && i + 1 < p.cur) {
             const int need = p.tk - 1 - i;
             const long long t0 = clock64();
-            const long long limit = (long long)(kWaitNs * 2.0);   // cycles at <= 2 GHz
+            const long long limit = p.wait_cycles;
             while ((seen = ld_acquire(&p.colprog[c])) < need) {
                 if (ld_acquire(p.err)) { ok = 0; break; }
                 if (clock64() - t0 > limit) { ok = 0; cause = 2; break; }
@@ -219,6 +219,9 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
     p.lazy_ws = a.lazy_ws;
     const int sms = device_sms();
     p.slots = a.slots; p.nslots = a.nslots; p.colprog = a.colprog; p.err = a.err;
+    // wait bound in SM clock cycles, counted at 2 cycles per ns (>= the
+    // B200's 1965 MHz maximum clock, so the bound is never shorter in time)
+    p.wait_cycles = (long long)(a.wait_ns * 2.0);
     for (int K = 0; K < 8; ++K) p.f2tab[K] = a.f2tab[K];
     p.lut32 = a.lut32;
 
@@ -402,6 +405,51 @@ __global__ void decode_kernel(const int16_t* __restrict__ tr, int tk, int tn, in
     }
     const int pos = tc_perm(t);
     W[(size_t)(16 * i + (pos >> 4)) * (16 * tn) + (16 * c + (pos & 15))] = lut[s];
+}
+
+// Self-check (quantize.py:849-853, :958-963): one thread per weight decodes
+// its state from the trellis window, as decode_kernel, and compares the
+// decoded value with the encoder's hatW (bit pattern) and, with states, the
+// state with the encoder's.  A warp adds its mismatch count once.
+__global__ void verify_kernel(const int16_t* __restrict__ tr, int tk, int tn, int K,
+                              const float* __restrict__ lut, const float* __restrict__ hatW,
+                              int ldw, const int32_t* __restrict__ states, int ld_states,
+                              int* __restrict__ bad) {
+    const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    bool miss = false;
+    if (gid < (size_t)tk * tn * 256) {
+        const size_t tile = gid / 256;
+        const int t = (int)(gid % 256);
+        const int i = (int)(tile / tn), c = (int)(tile % tn);
+        const uint16_t* w16 = reinterpret_cast<const uint16_t*>(tr) + tile * 16 * K;
+        const int nbits = 256 * K;
+        const int b0 = (t * K + K - 16 + nbits) % nbits;
+        uint32_t s = 0;
+        for (int j = 0; j < 16; ++j) {
+            const int q = (b0 + j) % nbits;
+            const int wi = q >> 5, bi = q & 31;
+            const uint32_t word = (uint32_t)w16[2 * wi] | ((uint32_t)w16[2 * wi + 1] << 16);
+            s = (s << 1) | ((word >> (31 - bi)) & 1u);
+        }
+        const int pos = tc_perm(t);
+        const float hw = hatW[(size_t)(16 * i + (pos >> 4)) * ldw + (16 * c + (pos & 15))];
+        miss = __float_as_uint(lut[s]) != __float_as_uint(hw);
+        if (states)
+            miss = miss || (uint32_t)(states[((size_t)i * ld_states + c) * 256 + t] & 0xFFFF) != s;
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, miss);
+    if ((threadIdx.x & 31) == 0 && m) atomicAdd(bad, __popc(m));
+}
+
+int launch_verify(const int16_t* tr, int tk, int tn, int K, const float* lut,
+                  const float* hatW, int ldw, const int32_t* states, int ld_states, int* bad,
+                  cudaStream_t stream) {
+    const size_t total = (size_t)tk * tn * 256;
+    if (total)
+        verify_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+            tr, tk, tn, K, lut, hatW, ldw, states, ld_states, bad);
+    note_launch();
+    return check_cuda(cudaGetLastError(), "verify launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
 int launch_pack(const int32_t* st, int nt, int K, int16_t* out, cudaStream_t stream) {

@@ -67,7 +67,7 @@ __device__ __forceinline__ void lazy_wait_dep(const LdlqTileParams& p, volatile 
     if (!p.Lfac || i + 1 >= p.cur) return;
     const int need = p.tk - 1 - i;
     const long long t0 = clock64();
-    const long long limit = (long long)(kWaitNs * 2.0);   // cycles at <= 2 GHz
+    const long long limit = p.wait_cycles;
     int seen;
     while ((seen = ld_acquire(&p.colprog[c])) < need) {
         if (ld_acquire(p.err)) { sc->ok = 0; return; }

@@ -28,6 +28,7 @@ struct LdlqTileParams {
     int* slots;             // [nslots] backpointer-slot ownership flags
     int nslots;
     int* err;               // error word (set on a wait time-out)
+    long long wait_cycles;  // bound of every dependency / slot wait (SM clock cycles)
     int nseg;
     int seg_c0[kMaxSeg + 1];     // segment column-tile starts, seg_c0[nseg] = tn
     int seg_K[kMaxSeg];
@@ -60,7 +61,7 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
     return v;
 }
 
-constexpr long long kWaitNs = 4000000000LL;   // 4 s bound on any dependency wait
+constexpr long long kWaitNs = 4000000000LL;   // default bound of any dependency wait: 4 s
 
 // Ticket -> (k-block i, column tile c, segment) of this launch: k-blocks from
 // `top` down, columns of the launch's segments in order within a block.

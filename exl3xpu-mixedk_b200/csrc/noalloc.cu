@@ -10,8 +10,15 @@
 // and first use on a device uploads the decode tables.
 //
 // How: the encoder's backpointer scratch (one 256-step slot per sequence) lives
-// in a fixed file-scope device array of kNoAllocScratchBytes (64 MiB) that every
-// GPU which loads this library holds until the process exits.  The decode values
+// in a fixed file-scope device array of kNoAllocScratchBytes (64 MiB).  The CUDA
+// runtime creates that array when it loads this library's device code on a GPU,
+// and the GPU keeps it until the process exits.  With lazy module loading (the
+// default since CUDA 12.2, CUDA_MODULE_LOADING=LAZY) that load happens inside
+// the first call on each device -- the cudaGetSymbolAddress of the set-up --
+// so that first call does take 64 MiB of device memory; with eager loading
+// every context that loads the library takes it at start-up, whether or not it
+// ever calls this entry point.  Callers that reserve the device's memory
+// should make one warm-up call per device first.  The decode values
 // are computed in the kernel from the code formulas instead of being read from
 // device tables, so no table has to be allocated either.  The caller passes the
 // targets and the output states, as for exl3b_tailbite.
@@ -26,8 +33,11 @@
 //    them one after another on one stream.  No part of the scratch has to start
 //    at zero: each backpointer row is written before it is read within a call.
 //  * the first call on each device does the set-up: it looks up the device
-//    address of the scratch array (cudaGetSymbolAddress) and raises the kernels'
-//    shared-memory limit.  Make that first call before any stream capture.
+//    address of the scratch array (cudaGetSymbolAddress, which under lazy
+//    loading also loads the module and so creates the 64 MiB array) and raises
+//    the kernels' shared-memory limit.  Make that first call before reserving
+//    the device's memory and before any stream capture; later calls allocate
+//    nothing.
 #include <mutex>
 
 #include "exl3b_internal.h"
@@ -131,7 +141,9 @@ int set_smem_limit() {
 }
 
 // Once per device, with it current: the scratch array's device address and the
-// kernels' shared-memory limit.  Allocates nothing.
+// kernels' shared-memory limit.  Calls no allocating routine itself, but under
+// lazy module loading the symbol lookup loads the module, which creates the
+// array.
 int noalloc_setup(int dev, uint8_t** out) {
     std::lock_guard<std::mutex> lk(g_na_mu);
     if (!g_na_ptr[dev]) {

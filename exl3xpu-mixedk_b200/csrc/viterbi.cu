@@ -76,6 +76,40 @@ tailbite_kernel(const float* __restrict__ X, int pivot, int margin,
             reinterpret_cast<const int32_t*>(smem + SM::OFF_ST)[t];
 }
 
+// Single Viterbi pass (quantize.py:218-320 viterbi): T <= 256 targets per
+// sequence (row-major X [nseq][T]), optional per-sequence pin `overlap`
+// (s_0 >> K and s_{T-1} mod 2^(16-K) both equal to it; values are taken mod
+// 2^(16-K)), and optional `back_from` >= 0: backpointers only for steps after
+// it, and only the state at step back_from is returned (states [nseq]).
+// Otherwise states [nseq][T].  Same trellis step and traceback as the
+// tail-biting encoder's passes (vit_pass), one CTA per sequence.
+template <int K>
+__global__ void __launch_bounds__(kVT, 1)
+viterbi_kernel(const float* __restrict__ X, int T, const int32_t* __restrict__ overlap,
+               int back_from, int32_t* __restrict__ states, uint8_t* __restrict__ bp_ws,
+               const uint4* __restrict__ f2tab) {
+    extern __shared__ __align__(16) char smem[];
+    using SM = VitSmem<K>;
+    using G = Geo<K>;
+    const int t = threadIdx.x;
+    const int seq = blockIdx.x;
+    __half2 f2[64];
+    vit_load_f2tab(f2, f2tab, t);
+    float* xs = reinterpret_cast<float*>(smem + SM::OFF_X);
+    if (t < T) xs[t] = X[(size_t)seq * T + t];
+    __syncthreads();
+    const int ov = overlap ? (overlap[seq] & (G::SPRE - 1)) : -1;
+    uint8_t* bp = bp_ws + (size_t)blockIdx.x * kSteps * G::BP_ROW;
+    int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST);
+    const int s = vit_pass<K>(f2, smem, 0, T, ov, back_from < 0 ? 0 : back_from,
+                              back_from < 0 ? st : nullptr, bp, t);
+    if (back_from < 0) {
+        if (t < T) states[(size_t)seq * T + t] = st[t];
+    } else if (t == 0) {
+        states[seq] = s;
+    }
+}
+
 
 template <int K>
 __global__ void __launch_bounds__(kLazyThreads, 1)
@@ -223,6 +257,48 @@ static int launch_lazy_k(const float* dX, int nseq, int pivot, int margin, int32
     note_launch();
     return check_cuda(cudaGetLastError(), "tailbite_lazy_kernel launch") ? RC_DEVICE_ERROR
                                                                        : RC_OK;
+}
+
+template <int K>
+static int launch_viterbi_k(const float* dX, int nseq, int T, const int32_t* dOverlap,
+                            int back_from, int32_t* dStates, uint8_t* ws, int grid,
+                            const uint4* f2tab, cudaStream_t stream) {
+    const int smem = VitSmem<K>::BYTES;
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev]) {
+        if (check_cuda(cudaFuncSetAttribute(viterbi_kernel<K>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                       "cudaFuncSetAttribute(viterbi)"))
+            return RC_DEVICE_ERROR;
+        attr_set[dev] = true;
+    }
+    const size_t per_seq = back_from < 0 ? (size_t)T : 1;
+    for (int s0 = 0; s0 < nseq; s0 += grid) {
+        const int n = nseq - s0 < grid ? nseq - s0 : grid;
+        viterbi_kernel<K><<<n, kVT, smem, stream>>>(
+            dX + (size_t)s0 * T, T, dOverlap ? dOverlap + s0 : nullptr, back_from,
+            dStates + (size_t)s0 * per_seq, ws, f2tab);
+        note_launch();
+        if (check_cuda(cudaGetLastError(), "viterbi_kernel launch")) return RC_DEVICE_ERROR;
+    }
+    return RC_OK;
+}
+
+int launch_viterbi(const float* dX, int nseq, int T, int K, const int32_t* dOverlap,
+                   int back_from, int32_t* dStates, uint8_t* ws, int grid,
+                   const uint4* f2tab, cudaStream_t stream) {
+    switch (K) {
+        case 2: return launch_viterbi_k<2>(dX, nseq, T, dOverlap, back_from, dStates, ws, grid, f2tab, stream);
+        case 3: return launch_viterbi_k<3>(dX, nseq, T, dOverlap, back_from, dStates, ws, grid, f2tab, stream);
+        case 4: return launch_viterbi_k<4>(dX, nseq, T, dOverlap, back_from, dStates, ws, grid, f2tab, stream);
+        case 5: return launch_viterbi_k<5>(dX, nseq, T, dOverlap, back_from, dStates, ws, grid, f2tab, stream);
+        case 6: return launch_viterbi_k<6>(dX, nseq, T, dOverlap, back_from, dStates, ws, grid, f2tab, stream);
+        case 7: return launch_viterbi_k<7>(dX, nseq, T, dOverlap, back_from, dStates, ws, grid, f2tab, stream);
+    }
+    set_error("K=%d outside 2..7", K);
+    return RC_BAD_K;
 }
 
 size_t lazy_region_bytes(int K) {

@@ -10,8 +10,13 @@ reference's quantize step can switch to this module:
     ldlq_viterbi       quantize.py:631-746
     quantize_seq_tailbite / viterbi / pack_states / unpack_states /
     decode_trellis / block_LDL / to_inner / from_inner / rotate_hessian /
-    get_lut / tensor_core_perm / sign_vec / hadamard128 / rel_mse /
-    hessian_weighted_err
+    had_left / had_right / get_lut / CODES / tensor_core_perm / sign_vec /
+    hadamard128 / rel_mse / hessian_weighted_err
+
+Like the reference, quantize_linear and quantize check every tensor they
+encode before returning it (quantize.py:849-853, :958-963): the packed
+trellis, decoded on device, must reproduce the encoder's output, or
+RuntimeError is raised.
 
 Every numerical step runs in hand-written CUDA kernels behind the C ABI of
 ``libexl3b200.so``; torch provides device memory, streams and host<->device
@@ -115,6 +120,20 @@ def get_lut(code: str, L: int = 16, device=None) -> torch.Tensor:
     return lut.to(device) if device is not None else lut
 
 
+def _code_decoder(code: str):
+    def decode(states: torch.Tensor) -> torch.Tensor:
+        lut = get_lut(code)
+        return lut.to(states.device)[states.long() & 0xFFFF]
+    return decode
+
+
+# The reference's optional code registry (quantize.py:44-49: name ->
+# (decode_fn, metadata)), filled here with the V=1 codes this package encodes:
+# decode_fn maps int states to their fp32 decode values.
+CODES = {name: (_code_decoder(name), {"V": 1, "L": 16, "code_id": cid})
+         for name, cid in native.CODE_IDS.items()}
+
+
 def _lut_rms(lut: torch.Tensor) -> torch.Tensor:
     return lut.double().square().mean().sqrt().float()      # quantize.py:778
 
@@ -159,6 +178,44 @@ def hadamard128(device=None, dtype=torch.float32) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ incoherence
+def _check_h(h):
+    """The reference passes the normalised block-128 Hadamard matrix around;
+    the kernels use butterflies, so any other matrix is refused."""
+    if h is None:
+        return
+    hc = h.detach().float().cpu()
+    if hc.shape != (128, 128) or not torch.equal(hc, hadamard128()):
+        raise ValueError("h must be hadamard128(): the CUDA transforms implement the "
+                         "normalised block-128 Sylvester Hadamard")
+
+
+def _had_axis(w: torch.Tensor, h, axis: int) -> torch.Tensor:
+    _check_h(h)
+    dev = _cuda_device(w.device)
+    _select(dev)
+    X = w.detach().to(dev, torch.float32).contiguous()
+    Y = torch.empty_like(X)
+    call("exl3b_hadamard_axis", X.data_ptr(), X.shape[0], X.shape[1], axis, Y.data_ptr(),
+         _stream(dev))
+    return Y.to(w.device)
+
+
+def had_left(w: torch.Tensor, h=None) -> torch.Tensor:
+    """quantize.py:135-139: block-128 Hadamard on the first (k) dim of
+    w [k, n] (k % 128 == 0), fp32, on the CUDA device; result on w's device."""
+    if w.dim() != 2 or w.shape[0] % 128:
+        raise ValueError(f"had_left: w {tuple(w.shape)} needs k % 128 == 0")
+    return _had_axis(w, h, 0)
+
+
+def had_right(w: torch.Tensor, h=None) -> torch.Tensor:
+    """quantize.py:142-146: block-128 Hadamard on the last (n) dim of
+    w [k, n] (n % 128 == 0)."""
+    if w.dim() != 2 or w.shape[1] % 128:
+        raise ValueError(f"had_right: w {tuple(w.shape)} needs n % 128 == 0")
+    return _had_axis(w, h, 1)
+
+
 def to_inner(w_orig: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor,
              h=None, device=None) -> torch.Tensor:
     """quantize.py:149-155: W_orig [k,n] -> B diag(1/suh) W diag(1/svh) B.
@@ -288,6 +345,55 @@ def _damp_f64(Gd: torch.Tensor, extra: float):
 
 
 # ------------------------------------------------------------------ Viterbi
+def _check_emit(dtype, emit_mode):
+    if emit_mode != "sq":
+        raise ValueError(f"emit_mode={emit_mode!r}: the CUDA encoder implements the "
+                         "reference's fp32 'sq' emit (quantize.py:255-260)")
+    if dtype not in (None, torch.float32):
+        raise ValueError(f"dtype={dtype}: the CUDA encoder accumulates path costs in fp32")
+
+
+def viterbi(X: torch.Tensor, lut: torch.Tensor, K: int, L: int = 16, V: int = 1,
+            overlap: torch.Tensor | None = None, dtype: torch.dtype = torch.float32,
+            back_from: int | None = None, compiled: bool = False,
+            emit_mode: str = "sq"):
+    """quantize.py:218-320: one trellis Viterbi pass on the CUDA encoder,
+    bit-exact with the reference's fp32 "sq" emit.  X [T, B] (T <= 256) ->
+    states int64 [T, B]; with `overlap` [B], s_0 >> K and s_{T-1} mod
+    2^(16-K) are pinned to it; with `back_from`, returns only the state at
+    step back_from ([B]).  Results on X's device."""
+    _check_K(K)
+    _check_emit(dtype, emit_mode)
+    if V != 1 or L != L_BITS:
+        raise ValueError("the CUDA encoder takes V=1, L=16 trellises")
+    T, B = X.shape
+    if not 1 <= T <= STEPS:
+        raise ValueError(f"T={T}: one pass covers 1..{STEPS} steps")
+    if back_from is not None and int(back_from) < 0:
+        raise ValueError(f"back_from={back_from} must be >= 0")
+    code = _code_of_lut(lut)
+    dev = _cuda_device(X.device)
+    _select(dev)
+    Xs = X.detach().to(dev, torch.float32).t().contiguous()        # [B][T]
+    ov = None
+    if overlap is not None:
+        ov_h = overlap.detach().reshape(-1).to("cpu", torch.int64)
+        if ov_h.numel() != B:
+            raise ValueError(f"overlap has {ov_h.numel()} entries for {B} sequences")
+        if B and (int(ov_h.min()) < 0 or int(ov_h.max()) >= (1 << (16 - K))):
+            raise ValueError(f"overlap values must lie in [0, 2^{16 - K})")
+        ov = ov_h.to(torch.int32).to(dev)
+    bf = -1 if back_from is None else int(back_from)
+    out = torch.empty((B, T) if bf < 0 else (B,), dtype=torch.int32, device=dev)
+    if B:
+        wsb = lib().exl3b_viterbi_workspace_bytes(B, int(K))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        call("exl3b_viterbi", Xs.data_ptr(), B, T, int(K), ops.code_id(code), _ptr(ov), bf,
+             out.data_ptr(), ws.data_ptr(), wsb, _stream(dev))
+    res = out.t() if bf < 0 else out
+    return res.long().to(X.device)
+
+
 def quantize_seq_tailbite(X: torch.Tensor, lut: torch.Tensor, K: int, L: int = 16,
                           V: int = 1, dtype: torch.dtype = torch.float32,
                           pivot: int | None = None, margin: int = 0,
@@ -295,6 +401,7 @@ def quantize_seq_tailbite(X: torch.Tensor, lut: torch.Tensor, K: int, L: int = 1
     """quantize.py:323-354 on the CUDA encoder.  X [T=256, B] -> states
     int64 [256, B] (on X's device), bit-exact with the reference's "sq" emit."""
     _check_K(K)
+    _check_emit(dtype, emit_mode)
     T, B = X.shape
     if T != STEPS or V != 1 or L != L_BITS:
         raise ValueError("the CUDA encoder takes 256-step V=1 L=16 sequences")
@@ -347,6 +454,50 @@ def decode_trellis(trellis: torch.Tensor, lut: torch.Tensor, K: int, k: int, n: 
     call("exl3b_decode_trellis", tr.data_ptr(), tk, tn, int(K), ops.code_id(code),
          out.data_ptr(), _stream(dev))
     return out.to(trellis.device)
+
+
+def _verify_async(trellis: torch.Tensor, hatW: torch.Tensor, K: int, code: str,
+                  bad: torch.Tensor, states: torch.Tensor | None = None):
+    """Queue the self-check of one encoded column segment (quantize.py:849-853,
+    :958-963) on the current stream: every weight decoded from `trellis`
+    [tk, tn, 16K] must equal `hatW` (a [k, 16 tn] view, row pitch
+    hatW.stride(0)) and, with `states` ([tk, tn, 256] view), every unpacked
+    state the encoder's.  Mismatches are added to the device int `bad`."""
+    tk, tn, _ = trellis.shape
+    dev = trellis.device
+    st_ptr, ld_st = 0, 0
+    if states is not None:
+        st_ptr, ld_st = states.data_ptr(), states.stride(0) // 256
+    call("exl3b_verify_trellis", trellis.data_ptr(), tk, tn, int(K), ops.code_id(code),
+         hatW.data_ptr(), hatW.stride(0), st_ptr, ld_st, bad.data_ptr(), _stream(dev))
+
+
+def _verify_raise(bad: torch.Tensor, what: str):
+    n = int(bad.item())
+    if n:
+        raise RuntimeError(f"{what}: decode != encoder output ({n} weights or states "
+                           "differ between the packed trellis and the encoder)")
+
+
+def verify_trellis(trellis: torch.Tensor, hatW: torch.Tensor, K: int,
+                   code: str = "exl3_mul1", states: torch.Tensor | None = None):
+    """The reference's per-tensor self-check (quantize.py:849-853): the packed
+    trellis [k/16, n/16, 16K] decodes to hatW [k, n] (inner domain, unit
+    scale) bit for bit and, when given, unpacks to `states` [k/16, n/16, 256];
+    raises RuntimeError otherwise.  Runs on the CUDA device."""
+    dev = _cuda_device(trellis.device)
+    _select(dev)
+    tr = trellis.detach().to(dev, torch.int16).contiguous()
+    hw = hatW.detach().to(dev, torch.float32).contiguous()
+    tk, tn, w = tr.shape
+    if w != 16 * K or hw.shape != (16 * tk, 16 * tn):
+        raise ValueError(f"trellis {tuple(tr.shape)} / hatW {tuple(hw.shape)} / K={K}")
+    st = None
+    if states is not None:
+        st = states.detach().to(dev, torch.int32).reshape(tk, tn, 256).contiguous()
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    _verify_async(tr, hw, K, code, bad, st)
+    _verify_raise(bad, "verify_trellis")
 
 
 # ------------------------------------------------------------------ LDLQ
@@ -541,9 +692,18 @@ def quantize_linear_fused(Ws: list, H_x: torch.Tensor | None, code: str = "exl3_
     hatW, trl, st, _ = _sweep(Wq, Lfac, list(Ks), widths, code, pv, margin, buf_cols,
                               progress=progress, want_states=keep_states)
     del Wq, Lfac
+    # self-check of every member (quantize.py:849-853), read at the sync below
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    c0 = 0
+    for j, m in enumerate(members):
+        w = m["m_out"]
+        _verify_async(trl[j], hatW[:, c0:c0 + w], Ks[j], code, bad,
+                      None if st is None else st[:, c0 // 16:(c0 + w) // 16])
+        c0 += w
 
     od = torch.device(out_device) if out_device is not None else dev
     wscales = torch.cat([m["Wscale_d"] for m in members]).tolist()   # one host sync
+    _verify_raise(bad, "quantize_linear")
     outs = []
     c0 = 0
     for j, mem in enumerate(members):
@@ -642,11 +802,14 @@ def quantize(W_transformed: torch.Tensor, U_upper: torch.Tensor | None,
             raise
     pivot = int(seed) % STEPS
     hatW, trl, _st, _ = _sweep(Wq, Lfac, [K], [m_out], code, pivot, margin, 128)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    _verify_async(trl[0], hatW, K, code, bad)          # quantize.py:958-963
     W_hat = torch.empty(m_out, k_in, dtype=torch.float32, device=dev)
     call("exl3b_transpose_scale", 1, hatW.data_ptr(), k_in, m_out, _ptr(sv_m), _ptr(su_m),
          scale.data_ptr(), W_hat.data_ptr(), None, s)
     od = W_transformed.device
     sc = float(scale.item())
+    _verify_raise(bad, "quantize")
     W_hat, tr = _out(W_hat, od), _out(trl[0], od)
     _out_done(dev, od)
     return W_hat, tr, sc

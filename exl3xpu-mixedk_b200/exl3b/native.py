@@ -38,6 +38,9 @@ SIGNATURES = {
     "exl3b_profile_begin": (None, []),
     "exl3b_profile_end": (I, [I, P, P, P]),
     "exl3b_device_init": (I, [I]),
+    "exl3b_set_wait_limit_ms": (I, [D]),
+    "exl3b_viterbi_workspace_bytes": (SZ, [I, I]),
+    "exl3b_viterbi": (I, [P, I, I, I, I, P, I, P, P, SZ, P]),
     "exl3b_tailbite_workspace_bytes": (SZ, [I, I]),
     "exl3b_tailbite": (I, [P, I, I, I, I, I, P, P, SZ, P]),
     "exl3b_tailbite_noalloc": (I, [P, I, I, I, I, I, P, P]),
@@ -64,6 +67,8 @@ SIGNATURES = {
                              P, SZ, P]),
     "exl3b_feedback_gemm_workspace_bytes": (SZ, [I, I, I]),
     "exl3b_feedback_gemm": (I, [I, I, I, P, I, P, I, P, I, P, SZ, P]),
+    "exl3b_verify_trellis": (I, [P, I, I, I, I, P, I, P, I, P, P]),
+    "exl3b_hadamard_axis": (I, [P, I, I, I, P, P]),
     "exl3b_pack_states": (I, [P, I, I, P, P]),
     "exl3b_unpack_states": (I, [P, I, I, P, P]),
     "exl3b_decode_trellis": (I, [P, I, I, I, I, P, P]),

@@ -3,10 +3,13 @@
 ``sys.path`` gives the same public API, computed by the B200 CUDA kernels of
 ``exl3b`` (see exl3b/api.py)."""
 from exl3b.api import (  # noqa: F401
+    CODES,
     block_LDL,
     decode_trellis,
     from_inner,
     get_lut,
+    had_left,
+    had_right,
     hadamard128,
     hessian_weighted_err,
     ldlq_viterbi,
@@ -22,4 +25,6 @@ from exl3b.api import (  # noqa: F401
     tensor_core_perm,
     to_inner,
     unpack_states,
+    verify_trellis,
+    viterbi,
 )

@@ -12,6 +12,11 @@
  *   quantize/viterbi_esimd.cpp:970-1005  xtq_vit_run
  *   quantize/quantize.py:611-628         _esimd_tailbite  (exl3b_tailbite)
  *   quantize/quantize.py:323-354         quantize_seq_tailbite
+ *   quantize/quantize.py:218-320         viterbi          (exl3b_viterbi)
+ *   quantize/quantize.py:135-146         had_left / had_right (exl3b_hadamard_axis)
+ *   quantize/quantize.py:849-853, 958-963  the per-tensor self-check asserts
+ *                                        (exl3b_verify_trellis)
+ * and the pipeline entry points below, each with its reference lines.
  */
 #ifndef EXL3B200_H
 #define EXL3B200_H
@@ -73,6 +78,15 @@ int exl3b_profile_end(int kind, double* ms_total, long long* launches, double* u
  * entry point initialises the current device). */
 int exl3b_device_init(int device);
 
+/* Bound, in milliseconds, of every device-side wait of the LDLQ sweep (a tile
+ * waiting for the tile below it in its column, a backpointer-slot claim); 0
+ * restores the default of 4000 ms.  A wait that runs out ends its kernel with
+ * an error block, and exl3b_ldlq_sweep returns EXL3B_DEVICE_ERROR with the
+ * cause in exl3b_last_error(); the context stays usable.  Applies to sweeps
+ * started afterwards, in every thread.  No counterpart in the reference (its
+ * native encoder has no cross-CTA waits). */
+int exl3b_set_wait_limit_ms(double ms);
+
 /* Workspace bytes exl3b_tailbite needs for (nseq, K) on the current device
  * (0 for invalid arguments). */
 size_t exl3b_tailbite_workspace_bytes(int nseq, int K);
@@ -90,6 +104,22 @@ int exl3b_tailbite(const float* dX, int nseq, int K, int code, int pivot,
                    int margin, int32_t* dStates, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/* Single Viterbi pass (viterbi, quantize.py:218-320), bit-exact with its fp32
+ * "sq" emit; the building block of the tail-biting encode.
+ *   dX        [nseq][T] fp32 targets, 1 <= T <= 256
+ *   dOverlap  [nseq] int32 or NULL: pins s_0 >> K and s_{T-1} mod 2^(16-K)
+ *             to overlap[b] (values taken mod 2^(16-K))
+ *   back_from -1: dStates [nseq][T] receives every state; >= 0: backpointers
+ *             are kept only for steps after back_from and dStates [nseq]
+ *             receives the state at step back_from (the state at T-1 when
+ *             back_from >= T-1), as the reference's back_from argument
+ *   workspace/workspace_bytes: exl3b_viterbi_workspace_bytes(nseq, K) bytes,
+ *             256-byte aligned, or NULL for library scratch. */
+size_t exl3b_viterbi_workspace_bytes(int nseq, int K);
+int exl3b_viterbi(const float* dX, int nseq, int T, int K, int code,
+                  const int32_t* dOverlap, int back_from, int32_t* dStates,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* Tail-biting encode that allocates no device memory.  No counterpart in the
  * reference: it is for callers that must not allocate device memory while
  * they run -- a process whose GPU memory belongs to another allocator (for
@@ -97,14 +127,18 @@ int exl3b_tailbite(const float* dX, int nseq, int K, int code, int pivot,
  * and treats later cudaMalloc calls as failures), or a loop that cannot take
  * the device-wide synchronisation cudaMalloc / cudaFree can cause.  Same
  * arguments and results as exl3b_tailbite, minus the workspace: the
- * backpointer scratch is a fixed 64 MiB device array inside the library
- * (held by every GPU that loads it until exit) and the decode values are
- * computed from the code formulas.  At most 64 (K = 2, 3), 128 (K = 4, 5),
- * 256 (K = 6) or 512 (K = 7) sequences per call; more returns
- * EXL3B_BAD_NSEQ.  All calls on a device share the scratch: calls that
- * overlap on the GPU race, so issue them in order on one stream.  The first
- * call on a device looks up the scratch address and sets kernel attributes
- * (no allocation); make it before any stream capture. */
+ * backpointer scratch is a fixed 64 MiB device array inside the library and
+ * the decode values are computed from the code formulas.  The array is
+ * created when the CUDA runtime loads the library's device code on a GPU and
+ * kept until the process exits: under lazy module loading (the default since
+ * CUDA 12.2) that is during the first call on each device, which therefore
+ * does take 64 MiB; under eager loading, every context that loads the library
+ * takes it at start-up.  Make one warm-up call per device before reserving
+ * the device's memory and before any stream capture; later calls allocate
+ * nothing.  At most 64 (K = 2, 3), 128 (K = 4, 5), 256 (K = 6) or 512 (K = 7)
+ * sequences per call; more returns EXL3B_BAD_NSEQ.  All calls on a device
+ * share the scratch: calls that overlap on the GPU race, so issue them in
+ * order on one stream. */
 int exl3b_tailbite_noalloc(const float* dX, int nseq, int K, int code, int pivot,
                            int margin, int32_t* dStates, void* stream);
 
@@ -252,6 +286,25 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
 size_t exl3b_feedback_gemm_workspace_bytes(int M, int N, int K);
 int exl3b_feedback_gemm(int M, int N, int K, const float* dA_T, int lda, const float* dB,
                         int ldb, float* dC, int ldc, void* ws, size_t ws_bytes,
+                        void* stream);
+
+/* Per-tensor self-check of an encoded column segment (the reference's
+ * asserts at quantize.py:849-853 and :958-963: pack/unpack round trip and
+ * decode == encoder output).  Adds to *dMismatch (device int, caller-zeroed)
+ * the number of weights whose value decoded from dTrellis [tk][tn][16K]
+ * through `code` differs (bit pattern) from dHatW [16 tk][ldw] (the
+ * segment's first column; ldw >= 16 tn) and, when dStates [tk][ld_states]
+ * [256] (int32, the segment's first tile; nullable) is given, the number of
+ * states unpacked from the trellis that differ from the encoder's. */
+int exl3b_verify_trellis(const int16_t* dTrellis, int tk, int tn, int K, int code,
+                         const float* dHatW, int ldw, const int32_t* dStates, int ld_states,
+                         int* dMismatch, void* stream);
+
+/* One-sided block-128 Hadamard (had_left / had_right, quantize.py:135-146) of
+ * X [rows][cols] fp32: axis 0 along rows (rows % 128 == 0, any cols), axis 1
+ * along columns (cols % 128 == 0, any rows); normalised by 1/sqrt(128).
+ * dY may equal dX. */
+int exl3b_hadamard_axis(const float* dX, int rows, int cols, int axis, float* dY,
                         void* stream);
 
 /* Bitstream (quantize.py:360-415): pack int32 states [ntiles][256] into

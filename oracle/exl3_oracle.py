@@ -329,6 +329,36 @@ def ldlq_viterbi_steps(Wq: np.ndarray, Lfac: np.ndarray | None, lut: np.ndarray,
         states.transpose(1, 0, 2))
 
 
+def ldlq_block_targets(Wq: np.ndarray, Lfac: np.ndarray, hatW: np.ndarray, i: int,
+                       E: np.ndarray | None = None):
+    """The encoder targets of k-block i of an LDLQ sweep, in fp64, given the
+    sweep's finished rows below it (quantize.py:676-686): every buffering of
+    the reference (intra-buffer term plus the cached `prod` of earlier
+    buffers, :680-682 and :742-744) sums the same terms,
+        WXWX_i = Wq[16i:16i+16] + Lfac[16(i+1):, 16i:16i+16]^T (Wq - hatW)[16(i+1):],
+    only in another fp32 order.  Returns (X [tn, 256] fp64 in sequence order
+    x[t] = WXWX[perm[t]], A [tn, 256] fp64: the same sum over absolute
+    values, which bounds the fp32 rounding of any summation order).  E, if
+    given, is the fp32 Wq - hatW (the reference's error term, :681), computed
+    once by a caller that checks several blocks."""
+    k, n = Wq.shape
+    perm = tensor_core_perm()
+    kp, np_ = perm // 16, perm % 16
+    tn = n // 16
+    r0, r1 = 16 * i, 16 * (i + 1)
+    Lb = Lfac[r1:, r0:r1].astype(np.float64)                 # [later, 16]
+    if E is None:
+        E = Wq - hatW
+    E = E[r1:].astype(np.float64)
+    W = Wq[r0:r1].astype(np.float64)
+    WX = W + Lb.T @ E
+    A = np.abs(W) + np.abs(Lb).T @ np.abs(E)
+
+    def gather(M):
+        return np.ascontiguousarray(M[kp].reshape(256, tn, 16)[np.arange(256), :, np_].T)
+    return gather(WX), gather(A)
+
+
 def ldlq_viterbi(Wq: np.ndarray, Lfac: np.ndarray | None, lut: np.ndarray,
                  K: int, L: int = 16, buf_cols: int = 128,
                  pivot: int | None = None, margin: int = 0,

@@ -167,3 +167,23 @@ def test_quantize_linear_ldlq(oracle, K):
     assert abs(herr - ref) <= 1e-4 * ref, (herr, ref)
     same = (r["trellis"] == g[f"ldlq_K{K}_trellis"]).all(-1).mean()
     assert same >= 0.95, same
+
+
+def test_ldlq_block_targets_match_the_sweep(oracle, mul1_lut):
+    """The fp64 LDLQ targets (quantize.py:676-686, used to check the GPU
+    sweep's feedback) agree with the oracle sweep's own fp32 targets, given
+    the same finished rows, to fp32 rounding of the sum of |terms|."""
+    rng = np.random.default_rng(0)
+    k, n = 192, 64
+    A = rng.standard_normal((k, k))
+    G = (A.T @ A / k + 0.1 * np.eye(k)).astype(np.float32)
+    G[np.diag_indices_from(G)] += np.float32(0.01) * np.mean(np.diag(G))
+    L, _ = oracle.block_LDL(G, 16)
+    L = L.astype(np.float32)
+    Wq = rng.standard_normal((k, n)).astype(np.float32)
+    seen = {}
+    hat, _ = oracle.ldlq_viterbi(Wq, L, mul1_lut, 3, nthreads=8,
+                                 on_launch=lambda i, X, s: seen.__setitem__(i, X))
+    for i in range(k // 16):
+        Xr, Ab = oracle.ldlq_block_targets(Wq, L, hat, i)
+        assert (np.abs(seen[i] - Xr) / Ab).max() <= 1e-5, i

@@ -153,3 +153,93 @@ def test_xtq_vit_run_lazy_batch(oracle, mul1_lut):
     assert rc == 0, native.last_error()
     ref = oracle.tailbite(X, mul1_lut, 4, pivot=128, margin=0, nthreads=NTHREADS)
     assert np.array_equal(out, ref)
+
+
+@pytest.fixture(scope="module")
+def xq():
+    import quantize as _xq     # the drop-in module (exl3xpu-mixedk_b200/quantize.py)
+    return _xq
+
+
+@pytest.mark.parametrize("K", (2, 4, 7))
+def test_single_pass_viterbi_vs_reference(xq, K):
+    """viterbi() (quantize.py:218-320) through the drop-in module against the
+    reference's own outputs: free boundary, a per-sequence overlap pin, and
+    back_from=40 on a 60-step sequence (the shortened first pass)."""
+    g = golden("viterbi")
+    X = torch.from_numpy(g["X_gauss"][:4].T.copy())          # [T=256, B=4]
+    lut = xq.get_lut("exl3_mul1")
+    st = xq.viterbi(X, lut, K, 16)
+    assert st.shape == (256, 4) and st.dtype == torch.int64
+    assert np.array_equal(st.t().numpy().astype(np.uint16), g[f"plain_K{K}"])
+    ov = torch.from_numpy(g[f"overlap_in_K{K}"])
+    st = xq.viterbi(X, lut, K, 16, overlap=ov)
+    assert np.array_equal(st.t().numpy().astype(np.uint16), g[f"overlap_K{K}"])
+    bf = xq.viterbi(X[:60], lut, K, 16, back_from=40)
+    assert bf.shape == (4,)
+    assert np.array_equal(bf.numpy().astype(np.uint16), g[f"backfrom40_K{K}"])
+
+
+@pytest.mark.parametrize("K", range(2, 8))
+def test_single_pass_viterbi_vs_oracle(xq, oracle, mul1_lut, K):
+    """Every K, sequence lengths 1..256, more sequences than SMs (several
+    waves), overlap pins, and back_from before, at and past the last step."""
+    rng = np.random.default_rng(500 + K)
+    lut = xq.get_lut("exl3_mul1")
+    for T, nseq in ((256, 170), (61, 7), (1, 3), (17, 5)):
+        X = rng.standard_normal((nseq, T)).astype(np.float32)
+        Xt = torch.from_numpy(X.T.copy())
+        st = xq.viterbi(Xt, lut, K).t().numpy()
+        assert np.array_equal(st, oracle.viterbi(X, mul1_lut, K)), (T, "plain")
+        ov = rng.integers(0, 1 << (16 - K), nseq)
+        st = xq.viterbi(Xt, lut, K, overlap=torch.from_numpy(ov)).t().numpy()
+        assert np.array_equal(st, oracle.viterbi(X, mul1_lut, K, overlap=ov)), (T, "overlap")
+        for bf in sorted({0, T // 2, T - 1, T + 5}):
+            got = xq.viterbi(Xt, lut, K, back_from=bf).numpy()
+            ref = oracle.viterbi_back_from(X, mul1_lut, K, 16, bf)
+            assert np.array_equal(got, ref), (T, "back_from", bf)
+
+
+def test_viterbi_rejects_what_it_cannot_encode(xq):
+    X = torch.zeros(257, 2)
+    lut = xq.get_lut("exl3_mul1")
+    with pytest.raises(ValueError):
+        xq.viterbi(X, lut, 4)                      # longer than one 256-step pass
+    with pytest.raises(ValueError):
+        xq.viterbi(X[:8], lut, 4, overlap=torch.tensor([0, 1 << 12]))
+    with pytest.raises(ValueError):
+        xq.viterbi(X[:8], lut, 4, emit_mode="gemm")
+    with pytest.raises(ValueError):
+        xq.viterbi(X[:8], torch.randn(65536), 4)   # not an EXL3 table
+
+
+def test_had_left_right_vs_reference_formula(xq):
+    """had_left / had_right (quantize.py:135-146) against the explicit
+    block-diagonal product in fp64, with the other axis not a multiple of 128."""
+    gen = torch.Generator().manual_seed(12)
+    h = xq.hadamard128()
+    for k, n in ((256, 40), (128, 300), (384, 128)):
+        w = torch.randn(k, n, generator=gen)
+        ref = (h.double() @ w.double().view(k // 128, 128, n)).view(k, n)
+        got = xq.had_left(w, h)
+        assert got.shape == (k, n) and got.device == w.device
+        assert ((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6
+    for k, n in ((40, 256), (300, 128), (128, 384)):
+        w = torch.randn(k, n, generator=gen)
+        ref = (w.double().view(k, n // 128, 128) @ h.double()).view(k, n)
+        got = xq.had_right(w)
+        assert ((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6
+    with pytest.raises(ValueError):
+        xq.had_left(torch.zeros(100, 128))
+    with pytest.raises(ValueError):
+        xq.had_right(torch.zeros(128, 128), torch.eye(128))
+
+
+def test_codes_registry(xq):
+    """CODES (quantize.py:44-49): name -> (decode_fn, metadata) for the codes
+    this package encodes; decode_fn reproduces get_lut."""
+    for name in ("exl3_mul1", "exl3_3inst", "exl3_mcg"):
+        fn, meta = xq.CODES[name]
+        assert meta["V"] == 1
+        s = torch.arange(0, 65536, 97)
+        assert torch.equal(fn(s), xq.get_lut(name)[s])
