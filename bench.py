@@ -14,7 +14,10 @@ mul1, quantize_linear defaults: pivot 128, margin 0), packing and W_hat.
           host->device copy of W and H and the device->host copy of the
           results inside every timed step
   N > 1 : one process per GPU, each quantizing its own projection (seeded per
-          rank, no collective on the data path): weak scaling
+          rank, no collective on the data path): weak scaling -- the layer-
+          sharded way a stack of projections runs.  "per_layer" adds the time
+          of ONE projection with its output columns split over the N ranks
+          (exl3b.shard; all-gather of the finished tensors included)
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config c2|c3|c4] [--K k]
@@ -238,6 +241,51 @@ def _workload(args, rank, dev):
     return label, METRIC, W.numel(), [W, H], step, {"k": args.dim, "n": args.dim, "K": K_BITS}
 
 
+def _split_leg(args, dev, world, local, rank, barrier):
+    """Per-layer time of ONE projection (the workload's, same seeds on every
+    rank) with its output columns split over the N ranks (exl3b.shard: each
+    rank transforms W and factors H itself, sweeps its 128-aligned column
+    range; the finished trellis and W_hat are NCCL all-gathered inside the
+    timed region).  CUDA events, max over ranks.  None for the fused c3
+    module (its columns span three segments of different K)."""
+    import torch
+    import torch.distributed as dist
+    from exl3b import shard, synth
+    if args.config == "c3" or args.dim != DIM:
+        return None
+    if args.config == "c4":
+        W, H = synth.config4(device=dev)
+        K = args.K
+    else:
+        W, H = synth.config2(device=dev)
+        K = K_BITS
+
+    def run():
+        return shard.quantize_linear_split(W, H, K=K, out_device=dev)
+    for _ in range(max(args.warmup, 1)):
+        run()
+    barrier()
+    s = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        r = run()
+    e1.record(s)
+    barrier()
+    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    cols = shard.column_ranges(W.shape[0], world)
+    del r
+    return {"split": "output columns of one projection, one 128-aligned range per rank; "
+                     "each rank transforms W and factors H itself; NCCL all-gather of "
+                     "the trellis and W_hat inside the timed region",
+            "n_gpus": world, "ms_per_layer": ms, "weights_per_s": W.numel() / (ms / 1e3),
+            "columns_per_rank": [b - a for a, b in cols],
+            "column_tiles_per_rank": [(b - a) // 16 for a, b in cols]}
+
+
 def _to_host(inp):
     if isinstance(inp, list):
         return [_to_host(x) for x in inp]
@@ -396,6 +444,9 @@ def main():
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms = float(t_max.item())
     value = world * weights / (ms / 1e3)
+    # per-layer time with one projection split over the ranks (N = 1: the
+    # step itself, one whole projection on one GPU)
+    per_layer = _split_leg(args, dev, world, local, rank, barrier) if world > 1 else None
 
     # ---- e2e: public API from pinned host buffers, copies inside the step
     ms_e2e = float("nan")
@@ -477,7 +528,10 @@ def main():
         "roofline": roofline,
         "kernels": kernels,
         "clocks": clocks,
-        "per_layer_s": ms / 1e3,
+        "per_layer_s": (per_layer["ms_per_layer"] / 1e3) if per_layer else ms / 1e3,
+        "per_layer": per_layer if per_layer else {
+            "split": "none: one whole projection per GPU (N = 1, or a fused module)",
+            "n_gpus": world, "ms_per_layer": ms, "weights_per_s": weights / (ms / 1e3)},
     }
     if world > 1:
         dist.barrier(device_ids=[local])

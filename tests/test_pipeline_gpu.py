@@ -449,7 +449,7 @@ def test_pipeline_raises_on_corrupted_trellis(xq, monkeypatch):
     with pytest.raises(RuntimeError, match="decode != encoder output"):
         xq.quantize_linear(W, H, K=3)
     with pytest.raises(RuntimeError, match="decode != encoder output"):
-        xq.quantize_linear_fused([W, W[:64].contiguous() * 2], H, Ks=[4, 6])
+        xq.quantize_linear_fused([W, W[:128].contiguous() * 2], H, Ks=[4, 6])
     with pytest.raises(RuntimeError, match="decode != encoder output"):
         xq.quantize(W * 0.05, None, "exl3_mul1", 5, seed=1)
     monkeypatch.setattr(api, "_sweep", real)
