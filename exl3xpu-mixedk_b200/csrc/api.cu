@@ -359,7 +359,7 @@ int xtq_vit_init(void) {
     const int idx = (int)env_ll("XTQ_VIT_DEVIDX", -1);
     if (idx >= 0) {
         if (idx >= n) {
-            fprintf(stderr, "xtq_vit: XTQ_VIT_DEVIDX=%d, %d gpus\n", idx, n);
+            fprintf(stderr, "exl3b xtq_vit_init: XTQ_VIT_DEVIDX=%d but only %d CUDA devices\n", idx, n);
             set_error("XTQ_VIT_DEVIDX=%d of %d devices", idx, n);
             return RC_BAD_DEVICE;
         }
@@ -386,7 +386,7 @@ int xtq_vit_run(const float* X, int nseq, const char* code, int margin,
         return RC_BAD_REQUEST;
     }
     if (nseq <= 0 || nseq > env_ll("XTQ_VIT_MAXSEQ", 4096)) {
-        fprintf(stderr, "xtq_vit: nseq %d over XTQ_VIT_MAXSEQ\n", nseq);
+        fprintf(stderr, "exl3b xtq_vit_run: %d sequences exceed XTQ_VIT_MAXSEQ\n", nseq);
         set_error("nseq %d out of range", nseq);
         return RC_BAD_NSEQ;
     }
@@ -394,7 +394,7 @@ int xtq_vit_run(const float* X, int nseq, const char* code, int margin,
     const TailbitePlan plan = tailbite_plan(nseq, K, st->sms);
     const size_t dev_bytes = (size_t)nseq * kSteps * 8 + plan.bytes;
     if ((long long)dev_bytes > env_ll("XTQ_VIT_MAXBYTES", 6LL << 30)) {
-        fprintf(stderr, "xtq_vit: nseq %d over XTQ_VIT_MAXBYTES\n", nseq);
+        fprintf(stderr, "exl3b xtq_vit_run: %d sequences need more device bytes than XTQ_VIT_MAXBYTES\n", nseq);
         set_error("nseq %d over XTQ_VIT_MAXBYTES", nseq);
         return RC_TOO_MANY_BYTES;
     }

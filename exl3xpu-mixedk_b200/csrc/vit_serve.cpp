@@ -75,12 +75,12 @@ int serve() {
         const size_t got = fread(&q, 1, sizeof(q), stdin);
         if (got == 0) return 0;                        // EOF: caller is done
         if (got != sizeof(q)) {
-            fprintf(stderr, "exl3b_vit serve: short request header (%zu bytes)\n", got);
+            fprintf(stderr, "exl3b_vit serve: request frame truncated after %zu of 48 bytes\n", got);
             return 1;
         }
         q.code[15] = 0;
         if (q.magic != kMagic) {
-            fprintf(stderr, "exl3b_vit serve: bad magic 0x%x\n", q.magic);
+            fprintf(stderr, "exl3b_vit serve: frame magic 0x%08x is not 0x58545156; closing\n", q.magic);
             return 1;
         }
         if (q.op == 0) return 0;
@@ -90,7 +90,7 @@ int serve() {
         }
         x.resize((size_t)q.nseq * 256);
         if (!read_all(x.data(), (size_t)q.xbytes)) {
-            fprintf(stderr, "exl3b_vit serve: short X read\n");
+            fprintf(stderr, "exl3b_vit serve: stream ended inside the request's target block\n");
             return 1;
         }
         states.resize((size_t)q.nseq * 256);

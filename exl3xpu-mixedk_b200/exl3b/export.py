@@ -16,10 +16,12 @@ diag(suh) B_k . W_inner . B_n diag(svh) -- is the dequantised weight.  The
 channel-scales path of quantize_linear already returns folded fp16 suh/svh;
 for the plain path the writer folds ``suh * Wscale`` (fp16).
 
-Assembly (export_exl3.py:83-149): every template safetensors shard is copied
-and each blob for a provided key is overwritten in place (the header is kept,
-so writing a template's own tensors back reproduces it byte for byte); every
-other file is copied verbatim; ARTIFACTS.sha256 is regenerated.
+Assembly (the output of the reference's export_exl3.py:83-149): every
+provided field is checked against its slot in the template's headers, then
+each template shard is streamed to the output with those slots' bytes taken
+from the fields (headers unchanged, so a template's own tensors written back
+reproduce it byte for byte); every other file is copied as is and the
+ARTIFACTS.sha256 manifest is rebuilt.
 
 Fused mixed-K modules (serve/patches/0002-vllm-plugin-mixed-k.patch:126-205):
 members of one fused module (q/k/v, gate/up) are written as separate tensors
@@ -33,6 +35,7 @@ import json
 import os
 import shutil
 import struct
+from dataclasses import dataclass
 from pathlib import Path
 
 import numpy as np
@@ -150,92 +153,131 @@ def unpack_fused(flat: torch.Tensor, k: int, n_sizes: list, Ks: list) -> list:
 
 
 # ------------------------------------------------------------------ assembly
-def collect_inputs(tensors_root) -> dict:
-    """key -> (dtype tag, shape, raw bytes) for every per-tensor file under
-    ROOT/L*/ (key = model.language_model.layers.{nn}.{module}.{field})."""
-    from safetensors import safe_open
-    out = {}
+@dataclass
+class Blob:
+    """One quantized field ready to be spliced into a template shard."""
+    key: str                 # model.language_model.layers.{nn}.{module}.{field}
+    tag: str                 # safetensors dtype tag, e.g. "I16"
+    shape: list
+    data: bytes
+
+
+def _quant_files(tensors_root):
+    """(layer index, module name, path) of every per-tensor file under
+    ROOT/L*/, the module taken from the .json metadata when there is one."""
     for st_path in sorted(Path(tensors_root).glob("L*/*.safetensors")):
-        nn = str(int(st_path.parent.name[1:]))
-        module = st_path.stem
-        jp = st_path.with_suffix(".json")
-        if jp.exists():
-            module = json.loads(jp.read_text()).get("module", module)
-        prefix = f"{LAYER_PREFIX}{nn}.{module}."
-        with safe_open(str(st_path), framework="np") as f:
-            present = set(f.keys())
+        layer = int(st_path.parent.name[1:])
+        meta = st_path.with_suffix(".json")
+        module = json.loads(meta.read_text()).get("module", st_path.stem) \
+            if meta.exists() else st_path.stem
+        yield layer, module, st_path
+
+
+def collect_inputs(tensors_root) -> dict:
+    """Every EXL3 field of the per-tensor files under ROOT, keyed by its name
+    in the model: key -> (dtype tag, shape, raw little-endian bytes)."""
+    from safetensors import safe_open
+    blobs = {}
+    for layer, module, path in _quant_files(tensors_root):
+        with safe_open(str(path), framework="np") as f:
+            names = set(f.keys())
+            absent = [q for q in QUANT_FIELDS if q not in names]
+            if absent:
+                raise KeyError(f"{path} lacks the field(s) {absent}; it holds {sorted(names)}")
             for field in QUANT_FIELDS:
-                if field not in present:
-                    raise KeyError(f"{st_path}: missing key {field!r} (has {sorted(present)})")
-                arr = f.get_tensor(field)
+                arr = np.ascontiguousarray(f.get_tensor(field))
                 tag = _ST_OF_NP.get(str(arr.dtype))
                 if tag is None:
-                    raise ValueError(f"{st_path}:{field} has unsupported dtype {arr.dtype}")
-                out[prefix + field] = (tag, list(arr.shape), np.ascontiguousarray(arr).tobytes())
-    return out
+                    raise ValueError(f"{path}: field {field!r} is {arr.dtype}, which the "
+                                     "EXL3 layout does not use")
+                key = f"{LAYER_PREFIX}{layer}.{module}.{field}"
+                blobs[key] = (tag, list(arr.shape), arr.tobytes())
+    return blobs
 
 
-def _sha256_tree(outdir: Path) -> None:
-    lines = []
-    for item in sorted(outdir.iterdir()):
-        if not item.is_file() or item.name == "ARTIFACTS.sha256":
-            continue
-        h = hashlib.sha256()
-        with open(item, "rb") as f:
-            while True:
-                buf = f.read(1 << 24)
+def _plan_patches(blobs: dict, weight_map: dict, template: Path) -> dict:
+    """shard name -> [(absolute byte offset, Blob)], every blob checked
+    against the template's header entry before anything is written.  A blob
+    must land on a tensor of the same dtype, shape and byte size."""
+    plan: dict = {}
+    headers: dict = {}
+    for key, (tag, shape, data) in blobs.items():
+        shard = weight_map.get(key)
+        if shard is None:
+            raise KeyError(f"{key}: not in template index -- the template model has no "
+                           "tensor of that name")
+        if shard not in headers:
+            headers[shard] = read_st_header(template / shard)
+        hdr, base = headers[shard]
+        slot = hdr[key]
+        if slot["dtype"] != tag or list(slot["shape"]) != list(shape):
+            what = "dtype" if slot["dtype"] != tag else "shape"
+            raise ValueError(f"{key}: {what} differs from the template's "
+                             f"({tag} {list(shape)} produced, {slot['dtype']} "
+                             f"{list(slot['shape'])} expected)")
+        lo, hi = slot["data_offsets"]
+        if hi - lo != len(data):
+            raise ValueError(f"{key}: {len(data)} bytes produced, the template's slot "
+                             f"holds {hi - lo}")
+        plan.setdefault(shard, []).append((base + lo, Blob(key, tag, list(shape), data)))
+    for patches in plan.values():
+        patches.sort(key=lambda p: p[0])
+    return plan
+
+
+def _write_patched(src: Path, dst: Path, patches: list, chunk: int = 1 << 24) -> None:
+    """Copy src to dst in one streaming pass, taking the bytes of each
+    (offset, blob) patch from the blob instead of the source."""
+    with open(src, "rb") as fi, open(dst, "wb") as fo:
+        pos = 0
+        for off, blob in patches + [(None, None)]:
+            stop = off if off is not None else None
+            while stop is None or pos < stop:
+                want = chunk if stop is None else min(chunk, stop - pos)
+                buf = fi.read(want)
                 if not buf:
                     break
-                h.update(buf)
-        lines.append(f"{h.hexdigest()}  {item.name}")
-    (outdir / "ARTIFACTS.sha256").write_text("\n".join(lines) + "\n")
+                fo.write(buf)
+                pos += len(buf)
+            if blob is not None:
+                fo.write(blob.data)
+                fi.seek(len(blob.data), os.SEEK_CUR)
+                pos += len(blob.data)
+
+
+def _write_manifest(outdir: Path) -> None:
+    """ARTIFACTS.sha256: one "<sha256>  <name>" line per file of outdir."""
+    entries = []
+    for item in sorted(p for p in outdir.iterdir()
+                       if p.is_file() and p.name != "ARTIFACTS.sha256"):
+        digest = hashlib.sha256()
+        with open(item, "rb") as f:
+            for block in iter(lambda: f.read(1 << 24), b""):
+                digest.update(block)
+        entries.append(f"{digest.hexdigest()}  {item.name}")
+    (outdir / "ARTIFACTS.sha256").write_text("\n".join(entries) + "\n")
 
 
 def export(tensors_root, template, outdir) -> int:
-    """Assemble a complete EXL3 model directory: the template with every
-    provided tensor's blob replaced in place.  Returns the number of blobs
-    replaced.  Raises on a key the template does not have, a dtype / shape /
-    size mismatch, or a key left unwritten."""
+    """Build a complete EXL3 model directory in OUTDIR from TEMPLATE with the
+    quantized fields under TENSORS_ROOT spliced into the template's shards at
+    their tensors' byte ranges (headers untouched, so the template's own
+    tensors written back reproduce it byte for byte).  Every other template
+    file is copied as is and the sha256 manifest is rebuilt.  All fields are
+    validated before the first byte is written; returns how many were
+    spliced."""
     template, outdir = Path(template), Path(outdir)
     weight_map = json.loads((template / "model.safetensors.index.json").read_text())["weight_map"]
-    inputs = collect_inputs(tensors_root)
-    by_shard: dict = {}
-    for key, val in inputs.items():
-        if key not in weight_map:
-            raise KeyError(f"input key {key} not in template index")
-        by_shard.setdefault(weight_map[key], {})[key] = val
+    plan = _plan_patches(collect_inputs(tensors_root), weight_map, template)
     outdir.mkdir(parents=True, exist_ok=True)
-    shards = sorted(set(weight_map.values()))
-    written = set()
-    for shard in shards:
-        src, dst = template / shard, outdir / shard
-        hdr, base = read_st_header(src)
-        repl = by_shard.get(shard, {})
-        for key, (tag, shape, raw) in repl.items():
-            ent = hdr[key]
-            if ent["dtype"] != tag:
-                raise ValueError(f"{key}: dtype {tag} != template {ent['dtype']}")
-            if list(ent["shape"]) != shape:
-                raise ValueError(f"{key}: shape {shape} != template {ent['shape']}")
-            lo, hi = ent["data_offsets"]
-            if hi - lo != len(raw):
-                raise ValueError(f"{key}: {len(raw)} bytes != template {hi - lo}")
-        shutil.copyfile(src, dst)
-        if repl:
-            with open(dst, "r+b") as f:
-                for key, (_tag, _shape, raw) in repl.items():
-                    f.seek(base + hdr[key]["data_offsets"][0])
-                    f.write(raw)
-                    written.add(key)
-    left = set(inputs) - written
-    if left:
-        raise RuntimeError(f"keys not written: {sorted(left)}")
-    shard_set = set(shards)
+    shards = set(weight_map.values())
+    for shard in sorted(shards):
+        _write_patched(template / shard, outdir / shard, plan.get(shard, []))
     for item in template.iterdir():
-        if item.is_file() and item.name not in shard_set and item.name != "ARTIFACTS.sha256":
+        if item.is_file() and item.name not in shards and item.name != "ARTIFACTS.sha256":
             shutil.copyfile(item, outdir / item.name)
-    _sha256_tree(outdir)
-    return len(written)
+    _write_manifest(outdir)
+    return sum(len(p) for p in plan.values())
 
 
 def extract_template(template, workdir, only_keys=None) -> tuple[Path, int]:
