@@ -81,22 +81,34 @@ def stored_fields(result: dict) -> dict:
             "svh": svh.half().contiguous()}
 
 
-def save_quantized(root, layer: int, module: str, result: dict,
-                   meta: dict | None = None) -> Path:
-    """Write ROOT/L{layer:02d}/{module}.safetensors (+ .json metadata) for one
-    quantized tensor.  Returns the safetensors path."""
-    from safetensors.torch import save_file
-    ldir = Path(root) / f"L{int(layer):02d}"
-    ldir.mkdir(parents=True, exist_ok=True)
-    path = ldir / f"{module}.safetensors"
-    save_file(stored_fields(result), str(path))
+def tensor_info(module: str, result: dict, meta: dict | None = None) -> dict:
+    """The .json metadata of one quantized tensor."""
     info = {"module": module, "K": int(result["K"]), "Wscale": float(result["Wscale"]),
             "code": result.get("code", "exl3_mul1"),
             "channel_scales": bool(result.get("channel_scales", False))}
     if meta:
         info.update(meta)
+    return info
+
+
+def save_fields(root, layer: int, module: str, fields: dict, info: dict) -> Path:
+    """Write already-stored fields (stored_fields) and their metadata as
+    ROOT/L{layer:02d}/{module}.safetensors + .json."""
+    from safetensors.torch import save_file
+    ldir = Path(root) / f"L{int(layer):02d}"
+    ldir.mkdir(parents=True, exist_ok=True)
+    path = ldir / f"{module}.safetensors"
+    save_file(fields, str(path))
     path.with_suffix(".json").write_text(json.dumps(info, sort_keys=True))
     return path
+
+
+def save_quantized(root, layer: int, module: str, result: dict,
+                   meta: dict | None = None) -> Path:
+    """Write ROOT/L{layer:02d}/{module}.safetensors (+ .json metadata) for one
+    quantized tensor.  Returns the safetensors path."""
+    return save_fields(root, layer, module, stored_fields(result),
+                       tensor_info(module, result, meta))
 
 
 def load_quantized(path) -> dict:

@@ -14,14 +14,29 @@ Within a layer, tensors that read the same activations share one Hessian and
 form one fused module (q/k/v, gate/up), quantized by quantize_linear_fused
 at their per-member K (synth.SC5_K by default).
 
-    torchrun --nproc-per-node 8 -m exl3b.stack --layers 64 --out DIR
+Inputs: seeded synthetic weights; Hessians either synthetic (seeded per layer
+and group) or read from a directory of captured input Grams in the
+reference's dump format (check_tensor_bitexact.py:25-30, 94-95): one
+safetensors file per layer and linear, key "H", the undamped [in, in] Gram,
+named L{layer}_{module}.safetensors after the group's first member (e.g.
+L2_mlp.gate_proj.safetensors for gate/up) or L{layer}_{group}.safetensors.
+
+Timing: the synthesis (or loading) of each group's inputs and its
+quantization are timed separately with CUDA events.  Finished tensors leave
+the device as their three stored EXL3 fields and are written to disk by a
+background thread, so the file I/O overlaps the next group's quantization.
+
+    torchrun --nproc-per-node 8 -m exl3b.stack --layers 64 --out DIR [--hessians HDIR]
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import queue
+import threading
 import time
+from pathlib import Path
 
 MODULE_NAMES = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj",
                 "o": "self_attn.o_proj", "gate": "mlp.gate_proj", "up": "mlp.up_proj",
@@ -35,34 +50,111 @@ def assign_layers(n_layers: int, world: int) -> list:
     return [list(range(r, n_layers, world)) for r in range(world)]
 
 
+class Writer:
+    """Background writer of per-tensor EXL3 files: submit() queues the stored
+    fields (CPU tensors) of one tensor, a thread writes them with
+    export.save_quantized; close() waits for the queue to drain and re-raises
+    the first write error."""
+
+    def __init__(self, root):
+        self.root = root
+        self.q: queue.Queue = queue.Queue(maxsize=16)
+        self.err = None
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        from . import export
+        while True:
+            item = self.q.get()
+            if item is None:
+                return
+            if self.err is None:
+                try:
+                    export.save_fields(self.root, *item)
+                except Exception as e:          # reported by close()
+                    self.err = e
+
+    def submit(self, layer: int, module: str, result: dict, meta: dict):
+        from . import export
+        # device -> host in the calling thread (its stream order); the file
+        # I/O in the writer thread
+        self.q.put((layer, module, export.stored_fields(result),
+                    export.tensor_info(module, result, meta)))
+
+    def close(self):
+        self.q.put(None)
+        self.t.join()
+        if self.err is not None:
+            raise self.err
+
+
+def hessian_path(hdir, layer: int, group: str, members: list) -> Path:
+    """The captured Gram of (layer, group) under hdir, in the reference's
+    naming: L{layer}_{module}.safetensors of the group's first member, or
+    L{layer}_{group}.safetensors."""
+    cands = [Path(hdir) / f"L{layer}_{MODULE_NAMES[members[0]]}.safetensors",
+             Path(hdir) / f"L{layer}_{group}.safetensors"]
+    for c in cands:
+        if c.exists():
+            return c
+    raise FileNotFoundError(f"no Hessian for layer {layer} group {group!r}: tried "
+                            f"{', '.join(str(c) for c in cands)}")
+
+
+def load_hessian(path, dim: int, device):
+    """Key "H" of a Gram dump: fp32 [dim, dim] on `device`."""
+    from safetensors.torch import load_file
+    H = load_file(str(path))["H"]
+    if tuple(H.shape) != (dim, dim):
+        raise ValueError(f"{path}: H is {tuple(H.shape)}, the group's input dim is {dim}")
+    import torch
+    return H.to(device=device, dtype=torch.float32)
+
+
 def quantize_layer(layer: int, device, Ks: dict | None = None, out_root=None,
-                   tensors: list | None = None) -> list:
+                   tensors: list | None = None, writer: Writer | None = None,
+                   hessian_dir=None) -> list:
     """Quantize one layer's tensors on `device`; returns per-tensor stats
-    (name, K, weights, Wscale, seconds).  Writes EXL3 files when out_root is
-    given."""
+    (name, K, weights, Wscale, seconds of quantization, seconds of input
+    synthesis / loading -- each group's time shared by weight).  Writes EXL3
+    files when out_root is given (through `writer` in the background, else
+    inline)."""
     import torch
 
     from . import api, export, synth
     Ks = dict(synth.SC5_K if Ks is None else Ks)
     stats = []
-    for group, dim, members in synth.STACK_GROUPS:
-        members = [m for m in members if tensors is None or m in tensors]
+    s = torch.cuda.current_stream(device)
+    for group, dim, group_members in synth.STACK_GROUPS:
+        members = [m for m in group_members if tensors is None or m in tensors]
         if not members:
             continue
-        t0 = time.time()
-        H = synth.hessian(dim, synth.stack_hessian_seed(layer, group), device)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(s)
+        if hessian_dir is not None:
+            H = load_hessian(hessian_path(hessian_dir, layer, group, group_members), dim,
+                             device)
+        else:
+            H = synth.hessian(dim, synth.stack_hessian_seed(layer, group), device)
         Ws = [synth.stack_weight(layer, m, device) for m in members]
+        ev[1].record(s)
         res = api.quantize_linear_fused(Ws, H, Ks=[Ks[m] for m in members], device=device,
                                         out_device=device)
-        torch.cuda.synchronize(device)
-        dt = time.time() - t0
+        ev[2].record(s)
+        ev[2].synchronize()
+        t_syn, t_q = ev[0].elapsed_time(ev[1]) / 1e3, ev[1].elapsed_time(ev[2]) / 1e3
+        tot = sum(w.numel() for w in Ws)
         for m, W, r in zip(members, Ws, res):
-            if out_root is not None:
-                export.save_quantized(out_root, layer, MODULE_NAMES[m], r,
-                                      meta={"group": group, "layer": layer})
+            meta = {"group": group, "layer": layer}
+            if writer is not None:
+                writer.submit(layer, MODULE_NAMES[m], r, meta)
+            elif out_root is not None:
+                export.save_quantized(out_root, layer, MODULE_NAMES[m], r, meta=meta)
             stats.append({"layer": layer, "tensor": m, "K": r["K"],
                           "weights": W.numel(), "Wscale": r["Wscale"],
-                          "seconds": dt * W.numel() / sum(w.numel() for w in Ws)})
+                          "seconds": t_q * W.numel() / tot,
+                          "synth_seconds": t_syn * W.numel() / tot})
         del H, Ws, res
     return stats
 
@@ -82,6 +174,9 @@ def main(argv=None) -> int:
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--out", default=None, help="EXL3 per-tensor output root (optional)")
     ap.add_argument("--tensors", default=None, help="comma list of tensors (default all)")
+    ap.add_argument("--hessians", default=None,
+                    help="directory of captured input Grams (L{layer}_{module}.safetensors, "
+                         "key H); default: seeded synthetic Hessians")
     a = ap.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -98,8 +193,12 @@ def main(argv=None) -> int:
     if world > 1:
         dist.barrier(device_ids=[local])
     torch.cuda.synchronize()
+    writer = Writer(a.out) if a.out else None
     ev0.record()
-    stats = run_rank(a.layers, rank, world, dev, a.out, tensors=tensors)
+    stats = run_rank(a.layers, rank, world, dev, a.out, tensors=tensors, writer=writer,
+                     hessian_dir=a.hessians)
+    if writer is not None:
+        writer.close()          # the rank's last files are on disk inside the timing
     ev1.record()
     torch.cuda.synchronize()
     ms = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
@@ -111,9 +210,14 @@ def main(argv=None) -> int:
         dist.destroy_process_group()
     if rank == 0:
         weights = sum(s["weights"] for s in stats)
+        q_s = sum(s["seconds"] for s in stats)
+        syn_s = sum(s["synth_seconds"] for s in stats)
         print(json.dumps({"layers": a.layers, "n_gpus": world, "tensors": len(stats),
                           "weights": weights, "seconds": float(ms.item()) / 1e3,
-                          "weights_per_s": weights / (float(ms.item()) / 1e3)}))
+                          "weights_per_s": weights / (float(ms.item()) / 1e3),
+                          "quantize_gpu_seconds_all_ranks": q_s,
+                          "input_synthesis_gpu_seconds_all_ranks": syn_s,
+                          "hessians": a.hessians or "synthetic"}))
     return 0
 
 

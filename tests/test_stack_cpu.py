@@ -69,3 +69,48 @@ def test_two_rank_gloo_stack_covers_every_tensor_once():
     assert len({part[0]["pid"] for part in gathered}) == world
     assert sum(s["weights"] for part in gathered for s in part) == \
         n_layers * synth.stack_weights_per_layer()
+
+
+def test_writer_thread_writes_what_inline_writes(tmp_path):
+    """The background writer produces the same files as a direct write."""
+    import torch
+    from exl3b import export
+    gen = torch.Generator().manual_seed(3)
+    r = {"trellis": torch.randint(-30000, 30000, (4, 2, 64), generator=gen).to(torch.int16),
+         "suh": torch.randn(64, generator=gen).half(), "svh": torch.randn(32, generator=gen).half(),
+         "Wscale": 0.75, "K": 4, "code": "exl3_mul1", "channel_scales": False}
+    export.save_quantized(tmp_path / "a", 3, "mlp.down_proj", r, meta={"group": "down"})
+    w = stack.Writer(tmp_path / "b")
+    w.submit(3, "mlp.down_proj", r, {"group": "down"})
+    w.close()
+    for suffix in (".safetensors", ".json"):
+        a = (tmp_path / "a" / "L03" / f"mlp.down_proj{suffix}").read_bytes()
+        b = (tmp_path / "b" / "L03" / f"mlp.down_proj{suffix}").read_bytes()
+        assert a == b, suffix
+
+
+def test_writer_reports_a_failed_write(tmp_path):
+    import torch
+    blocker = tmp_path / "file"
+    blocker.write_text("x")                      # a file where the layer dir should go
+    w = stack.Writer(blocker)
+    r = {"trellis": torch.zeros(1, 1, 32, dtype=torch.int16), "suh": torch.ones(16).half(),
+         "svh": torch.ones(16).half(), "Wscale": 1.0, "K": 2}
+    w.submit(0, "mlp.up_proj", r, {})
+    with pytest.raises(OSError):
+        w.close()
+
+
+def test_hessian_files_in_the_reference_naming(tmp_path):
+    import torch
+    from safetensors.torch import save_file
+    save_file({"H": torch.eye(8)}, str(tmp_path / "L2_mlp.gate_proj.safetensors"))
+    save_file({"H": torch.eye(4)}, str(tmp_path / "L3_down.safetensors"))
+    p = stack.hessian_path(tmp_path, 2, "mlp", ["gate", "up"])
+    assert p.name == "L2_mlp.gate_proj.safetensors"
+    assert stack.hessian_path(tmp_path, 3, "down", ["down"]).name == "L3_down.safetensors"
+    with pytest.raises(FileNotFoundError):
+        stack.hessian_path(tmp_path, 4, "o", ["o"])
+    assert torch.equal(stack.load_hessian(p, 8, "cpu"), torch.eye(8))
+    with pytest.raises(ValueError):
+        stack.load_hessian(p, 16, "cpu")
