@@ -364,25 +364,42 @@ __global__ void pack_kernel(const int32_t* __restrict__ st, int nt, int K,
     out[tile * 16 * K + 2 * w + 1] = (int16_t)(word >> 16);
 }
 
-// unpack_states (quantize.py:381-402): state t = the 16-bit circular window
-// of the 256K-bit stream ending at bit (t+1)K.
+// State t of a tile (quantize.py:381-402): the 16-bit circular window of
+// its 256K-bit stream ending at bit (t+1)K.  Stream bit q is bit 31 - (q & 31)
+// of u32 word q >> 5, a word being int16 halves (low half first); the window
+// lies in words b0 >> 5 and the next one (circularly), so two words, read as
+// four 16-bit halves, give it with one 64-bit shift.
+__device__ __forceinline__ uint32_t tile_state(const uint16_t* __restrict__ w16, int K, int t) {
+    const int nbits = 256 * K;
+    int b0 = t * K + K - 16;
+    if (b0 < 0) b0 += nbits;
+    const int wi = b0 >> 5, bi = b0 & 31;
+    const int wj = (wi + 1 == 8 * K) ? 0 : wi + 1;
+    const uint32_t a = (uint32_t)__ldg(w16 + 2 * wi) | ((uint32_t)__ldg(w16 + 2 * wi + 1) << 16);
+    const uint32_t b = (uint32_t)__ldg(w16 + 2 * wj) | ((uint32_t)__ldg(w16 + 2 * wj + 1) << 16);
+    const uint64_t v = ((uint64_t)a << 32) | b;
+    return (uint32_t)(v >> (48 - bi)) & 0xFFFFu;
+}
+
+// unpack_states: trellis [nt][16K] -> states int32 [nt][256]
 __global__ void unpack_kernel(const int16_t* __restrict__ tr, int nt, int K,
                               int32_t* __restrict__ st) {
     const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (size_t)nt * 256) return;
     const size_t tile = gid / 256;
-    const int t = (int)(gid % 256);
     const uint16_t* w16 = reinterpret_cast<const uint16_t*>(tr) + tile * 16 * K;
-    const int nbits = 256 * K;
-    const int b0 = (t * K + K - 16 + nbits) % nbits;
-    uint32_t s = 0;
-    for (int j = 0; j < 16; ++j) {
-        const int q = (b0 + j) % nbits;
-        const int wi = q >> 5, bi = q & 31;
-        const uint32_t word = (uint32_t)w16[2 * wi] | ((uint32_t)w16[2 * wi + 1] << 16);
-        s = (s << 1) | ((word >> (31 - bi)) & 1u);
-    }
-    st[gid] = (int32_t)s;
+    st[gid] = (int32_t)tile_state(w16, K, (int)(gid % 256));
+}
+
+// Element (r, cc) of a [16 tk][16 tn] matrix -> (tile, step t): the inverse
+// of tc_perm inside tile (r / 16, cc / 16).  One thread per element in
+// row-major order keeps the matrix side of decode and verify coalesced.
+__device__ __forceinline__ void elem_tile_step(size_t gid, int tn, size_t& tile, int& t) {
+    const int n = 16 * tn;
+    const size_t r = gid / n;
+    const int cc = (int)(gid - r * n);
+    tile = (r >> 4) * (size_t)tn + (cc >> 4);
+    t = tc_perm_inv((int)(r & 15), cc & 15);
 }
 
 // decode_trellis (quantize.py:405-415): trellis [tk][tn][16K] -> W [k][n]
@@ -390,27 +407,17 @@ __global__ void decode_kernel(const int16_t* __restrict__ tr, int tk, int tn, in
                               const float* __restrict__ lut, float* __restrict__ W) {
     const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (size_t)tk * tn * 256) return;
-    const size_t tile = gid / 256;
-    const int t = (int)(gid % 256);
-    const int i = (int)(tile / tn), c = (int)(tile % tn);
+    size_t tile;
+    int t;
+    elem_tile_step(gid, tn, tile, t);
     const uint16_t* w16 = reinterpret_cast<const uint16_t*>(tr) + tile * 16 * K;
-    const int nbits = 256 * K;
-    const int b0 = (t * K + K - 16 + nbits) % nbits;
-    uint32_t s = 0;
-    for (int j = 0; j < 16; ++j) {
-        const int q = (b0 + j) % nbits;
-        const int wi = q >> 5, bi = q & 31;
-        const uint32_t word = (uint32_t)w16[2 * wi] | ((uint32_t)w16[2 * wi + 1] << 16);
-        s = (s << 1) | ((word >> (31 - bi)) & 1u);
-    }
-    const int pos = tc_perm(t);
-    W[(size_t)(16 * i + (pos >> 4)) * (16 * tn) + (16 * c + (pos & 15))] = lut[s];
+    W[gid] = __ldg(lut + tile_state(w16, K, t));
 }
 
-// Self-check (quantize.py:849-853, :958-963): one thread per weight decodes
-// its state from the trellis window, as decode_kernel, and compares the
-// decoded value with the encoder's hatW (bit pattern) and, with states, the
-// state with the encoder's.  A warp adds its mismatch count once.
+// Self-check (quantize.py:849-853, :958-963): one thread per weight, in
+// hatW's row-major order, decodes its state from the trellis window and
+// compares the decoded value with the encoder's hatW (bit pattern) and, with
+// states, the state with the encoder's.  A warp adds its mismatch count once.
 __global__ void verify_kernel(const int16_t* __restrict__ tr, int tk, int tn, int K,
                               const float* __restrict__ lut, const float* __restrict__ hatW,
                               int ldw, const int32_t* __restrict__ states, int ld_states,
@@ -418,24 +425,18 @@ __global__ void verify_kernel(const int16_t* __restrict__ tr, int tk, int tn, in
     const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     bool miss = false;
     if (gid < (size_t)tk * tn * 256) {
-        const size_t tile = gid / 256;
-        const int t = (int)(gid % 256);
-        const int i = (int)(tile / tn), c = (int)(tile % tn);
+        size_t tile;
+        int t;
+        elem_tile_step(gid, tn, tile, t);
         const uint16_t* w16 = reinterpret_cast<const uint16_t*>(tr) + tile * 16 * K;
-        const int nbits = 256 * K;
-        const int b0 = (t * K + K - 16 + nbits) % nbits;
-        uint32_t s = 0;
-        for (int j = 0; j < 16; ++j) {
-            const int q = (b0 + j) % nbits;
-            const int wi = q >> 5, bi = q & 31;
-            const uint32_t word = (uint32_t)w16[2 * wi] | ((uint32_t)w16[2 * wi + 1] << 16);
-            s = (s << 1) | ((word >> (31 - bi)) & 1u);
+        const uint32_t s = tile_state(w16, K, t);
+        const size_t r = gid / (16 * tn);
+        const float hw = hatW[r * (size_t)ldw + (gid - r * 16 * tn)];
+        miss = __float_as_uint(__ldg(lut + s)) != __float_as_uint(hw);
+        if (states) {
+            const size_t i = tile / tn, c = tile - i * tn;
+            miss = miss || (uint32_t)(states[(i * ld_states + c) * 256 + t] & 0xFFFF) != s;
         }
-        const int pos = tc_perm(t);
-        const float hw = hatW[(size_t)(16 * i + (pos >> 4)) * ldw + (16 * c + (pos & 15))];
-        miss = __float_as_uint(lut[s]) != __float_as_uint(hw);
-        if (states)
-            miss = miss || (uint32_t)(states[((size_t)i * ld_states + c) * 256 + t] & 0xFFFF) != s;
     }
     const unsigned m = __ballot_sync(0xffffffffu, miss);
     if ((threadIdx.x & 31) == 0 && m) atomicAdd(bad, __popc(m));

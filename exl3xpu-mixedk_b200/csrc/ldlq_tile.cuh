@@ -55,6 +55,13 @@ __device__ __forceinline__ int tc_perm(int t) {
     return row * 16 + col;
 }
 
+// (row, col) in the 16x16 tile -> sequence step t, the inverse of tc_perm
+__device__ __forceinline__ int tc_perm_inv(int row, int col) {
+    const int tt = (col & 7) * 4 + ((row & 7) >> 1);
+    const int q = (row & 1) | ((row >> 3) << 1) | ((col >> 3) << 2);
+    return tt * 8 + q;
+}
+
 __device__ __forceinline__ int ld_acquire(const int* p) {
     int v;
     asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
