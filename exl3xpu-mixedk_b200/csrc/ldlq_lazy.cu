@@ -40,6 +40,7 @@ struct LazyTileSmem {
     static constexpr int OFF_GATHER = OFF_WX + 1024;            // feedback rows
     static constexpr int OFF_SCHED = OFF_GATHER + kGatherStageBytes;
     static constexpr int BYTES = OFF_SCHED + (int)((sizeof(LazySched) + 15) / 16 * 16);
+    static_assert(BYTES <= 227 * 1024, "shared memory of one CTA");
 };
 
 // thread 0: take the next ticket into `slot` (got = 0 when the launch is done)
