@@ -366,7 +366,7 @@ def run_reference(args, rank):
                                    "LDL excluded (<1% of the CPU time)"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    _emit(line)
     return 0
 
 
@@ -546,11 +546,35 @@ def main():
                       "warm-up block, oracle C/numpy restatement, all host threads; "
                       "one-off rotation and LDL excluded (<1% of CPU time)"}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        _emit(line)
     if world > 1:
         dist.destroy_process_group()
     return 0
 
 
+def _stdout_for_json() -> int:
+    """Keep stdout for the one JSON line: duplicate the real stdout and point
+    file descriptor 1 at stderr, so that whatever the native libraries write
+    there (NCCL's version banner at communicator set-up, library logs) lands
+    on stderr.  Returns the duplicated descriptor."""
+    sys.stdout.flush()
+    fd = os.dup(1)
+    os.dup2(2, 1)
+    return fd
+
+
+_JSON_FD = None
+
+
+def _emit(line: dict):
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
+
 if __name__ == "__main__":
+    _JSON_FD = _stdout_for_json()
     sys.exit(main())
