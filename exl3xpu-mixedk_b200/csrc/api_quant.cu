@@ -337,7 +337,9 @@ static size_t sweep_ctrl_bytes(int tn) {
 }
 
 static size_t sweep_lazy_bytes(int kmin) {
-    return align256((size_t)device_sms() * 2 * lazy_region_bytes(kmin));
+    size_t r = 0;                        // the largest region of any K >= kmin
+    for (int K = kmin; K <= 7; ++K) r = lazy_region_bytes(K) > r ? lazy_region_bytes(K) : r;
+    return align256((size_t)device_sms() * 2 * r);
 }
 
 size_t exl3b_ldlq_workspace_bytes(int k, int n, int kmin, int use_ldlq) {

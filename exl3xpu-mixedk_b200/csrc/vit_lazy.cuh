@@ -57,12 +57,28 @@ constexpr int kLazyThreads = kVT + 32;   // 16 forward warps + the job warp
 template <int K>
 struct Lazy {
     using G = Geo<K>;
-    static constexpr int ROWS = kSteps - 1;                       // rows 1..254 used
     static constexpr int ROW_BYTES = G::SPRE * 4;                 // one best array
-    static constexpr size_t REGION = (size_t)ROWS * ROW_BYTES;    // bytes per tile region
     static constexpr int NPL = G::NC > 32 ? G::NC / 32 : 1;       // candidates per lane
     // rows by TMA bulk store from a shared-memory ring (else by the threads)
     static constexpr bool BULK = K <= 4;
+    // K = 2 (64 KB rows, whose writes bound the pass at the HBM rate): only
+    // the even rows are stored (row q at q / 2); the traceback rebuilds the 4
+    // entries it needs of an odd row q from row q - 1 with the forward step's
+    // fp32 operations (16 candidates over the job warp's lanes).  Measured on
+    // the standalone encoder at 20 tiles per SM: K = 2 0.723 -> 0.593 ms per
+    // tile-slot; the same scheme at K = 3 (64 candidates) and K = 4 (256)
+    // measured 2% and 20% slower: their rows cost less than the longer
+    // traceback.
+#ifndef EXL3B_LAZY_HALF_ROWS
+#define EXL3B_LAZY_HALF_ROWS 1
+#endif
+    static constexpr bool HALF = K == 2 && EXL3B_LAZY_HALF_ROWS;
+    static constexpr int ROWS = HALF ? kSteps / 2 : kSteps - 1;   // row slots (q <= 254)
+    static constexpr size_t REGION = (size_t)ROWS * ROW_BYTES;    // bytes per tile region
+    // half-row rebuild: (w, w') candidate pairs, per lane, lanes per w
+    static constexpr int PAIRS = G::NC * G::NC;
+    static constexpr int CPL = PAIRS > 32 ? PAIRS / 32 : 1;
+    static constexpr int GL = PAIRS > 32 ? 32 / G::NC : G::NC;
     // the ring of best arrays (64 KB: K = 2: 2, K = 3: 2, K = 4: 4; two when
     // the threads store the rows) and the rows per bulk copy (half the ring,
     // aligned: a batch's arrays are adjacent)
@@ -157,21 +173,48 @@ __device__ __forceinline__ void tb_job_run(char* smem, const float* __restrict__
     const float* xs = reinterpret_cast<const float*>(smem + SM::OFF_X) + 256 * slot;
     int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST) + 256 * slot;
     const float INF = __int_as_float(0x7f800000);
+    using L = Lazy<K>;
     for (; r > stop; --r) {
         const int j = (s & 0xFFFF) >> K;      // states are 16-bit
         const int m = j >> K;
         const int q = r - 1;
-        const float* row = rows + (size_t)q * G::SPRE;
+        const float* row = rows + (size_t)(L::HALF ? (q >> 1) : q) * G::SPRE;
         const float x = xs[(q - rol) & 255];
+        // odd row q of a half-row region: lane group w (GL lanes) rebuilds
+        // best_q[m + w P] = min_w' fl(fl(f(s') - x_{q-1})^2) + best_{q-1}[s' >> K],
+        // s' = m + w P + w' 2^(16-K), from row q - 1 (the boundary mask when
+        // q - 1 = 0); lane w then takes its group's value
+        float bh = INF;
+        if (L::HALF && (q & 1)) {
+            const float xp = xs[(q - 1 - rol) & 255];
+            const float* rp = rows + (size_t)((q - 1) >> 1) * G::SPRE;
+            const int w = lane / L::GL;
+            if (w < G::NC) {
+#pragma unroll
+                for (int k = 0; k < L::CPL; ++k) {
+                    const int sp = m + w * G::P + ((((lane % L::GL) * L::CPL) + k) << (16 - K));
+                    const int pi = sp >> K;
+                    const float bp = (q == 1) ? ((overlap < 0 || pi == overlap) ? 0.0f : INF)
+                                              : __ldcg(rp + G::baddr(pi));
+                    const float d = __fsub_rn(__ldg(lut32 + sp), xp);
+                    bh = fminf(bh, __fadd_rn(__fmul_rn(d, d), bp));
+                }
+            }
+#pragma unroll
+            for (int off = 1; off < L::GL; off <<= 1)
+                bh = fminf(bh, __shfl_xor_sync(0xffffffffu, bh, off));
+            bh = __shfl_sync(0xffffffffu, bh, (lane < G::NC ? lane : 0) * L::GL);
+        }
         uint32_t kc = 0xFFFFFFFFu;      // this lane's best cost bits, first index
         uint32_t kw = 0xFFFFFFFFu;
 #pragma unroll
-        for (int k = 0; k < Lazy<K>::NPL; ++k) {
+        for (int k = 0; k < L::NPL; ++k) {
             const int w = lane + 32 * k;
             if (w < G::NC) {
                 const int idx = m + w * G::P;
                 const float b = (q == 0) ? ((overlap < 0 || idx == overlap) ? 0.0f : INF)
-                                         : __ldcg(row + (Lazy<K>::BULK ? G::baddr(idx) : idx));
+                              : (L::HALF && (q & 1)) ? bh
+                              : __ldcg(row + (L::BULK ? G::baddr(idx) : idx));
                 const float d = __fsub_rn(__ldg(lut32 + j + (w << (16 - K))), x);
                 const uint32_t c = __float_as_uint(__fadd_rn(__fmul_rn(d, d), b));
                 if (c < kc) { kc = c; kw = (uint32_t)w; }
@@ -255,12 +298,13 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
     asm volatile("ld.volatile.shared.f32 %0, [%1];" : "=f"(zr)
                  : "r"((uint32_t)__cvta_generic_to_shared(zword)));
 
-    // rows the traceback reads: best_q, q in [max(stop, 1), nsteps - 2].
+    // rows the traceback reads: best_q, q in [max(stop, 1), nsteps - 2]
+    // (half rows: the even q of [lo & ~1, hi]).
     // Step i writes best_{i+1} into ring slot (i + 1) % RING.  Rows go out in
     // aligned batches of BATCH (rows b BATCH .. b BATCH + BATCH - 1, clipped to
-    // [lo, hi]; adjacent slots): when step i completes a batch, every thread
-    // fences its writes to the async proxy before the step barrier and thread
-    // 0 issues one bulk copy after it.  Before every step barrier thread 0
+    // [lo, hi]; adjacent slots; half rows: one even row per copy): when step i
+    // completes a batch, every thread fences its writes to the async proxy
+    // before the step barrier and thread 0 issues one bulk copy after it.  Before every step barrier thread 0
     // waits until the copies issued so far have read their slots; the
     // earliest reuse of a batch's slot is RING - BATCH >= 1 steps after that.
     const int lo = max(stop, 1), hi = nsteps - 2;
@@ -290,14 +334,23 @@ __device__ __forceinline__ int lazy_pass(const __half2 (&f2)[64], char* smem, in
             Bn = ring + ((i + 1) & (L::RING - 1)) * BB;
             const int q = i + 1;                  // the row this step writes
             vit_step<K, false>(f2, x, Bc, Bn, t, zr);
-            const bool flush = q >= lo && q <= hi && ((q % L::BATCH) == L::BATCH - 1 || q == hi);
+            // half rows: the even q in [lo & ~1, hi] (q >= 2), one per copy
+            const bool flush = L::HALF ? ((q & 1) == 0 && q >= 2 && q >= (lo & ~1) && q <= hi)
+                                       : (q >= lo && q <= hi &&
+                                          ((q % L::BATCH) == L::BATCH - 1 || q == hi));
             if (flush) row_fence_shared();        // this thread's writes -> async proxy
             if (t == 0) row_copies_read();        // earlier copies have read their slots
             asm volatile("bar.sync 1, %0;" :: "r"(kVT) : "memory");
             if (flush && t == 0) {
-                const int first = max(q - q % L::BATCH, lo);
-                row_copy(rows + (size_t)first * G::SPRE, ring + (first & (L::RING - 1)) * BB,
-                         (q - first + 1) * L::ROW_BYTES);
+                if (L::HALF) {
+                    row_copy(rows + (size_t)(q >> 1) * G::SPRE, ring + (q & (L::RING - 1)) * BB,
+                             L::ROW_BYTES);
+                } else {
+                    const int first = max(q - q % L::BATCH, lo);
+                    row_copy(rows + (size_t)first * G::SPRE,
+                             ring + (first & (L::RING - 1)) * BB,
+                             (q - first + 1) * L::ROW_BYTES);
+                }
             }
         }
         Bc = ring + ((nsteps - 1) & (L::RING - 1)) * BB;
