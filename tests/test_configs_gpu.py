@@ -141,3 +141,66 @@ def test_config4_parity(K):
     _check_blocks(oracle, _sampled(tk, per_buffer=False, extra=(tk - 1, tk - 17, 600, 545, 31, 0)),
                   [(0, 320, K)], Wq, Lfac, hatW, st, X)
     api.verify_trellis(trl[0], hatW, K, states=st)
+
+
+def _check_sampled(oracle, blocks, segs, Wq, Lfac, hatW, st, X, per_seg=96):
+    """_check_blocks on a spread of at most `per_seg` column tiles of every
+    segment (wide fused modules: the oracle re-encodes a sample of each
+    sampled k-block instead of all of its tiles; columns never interact, so
+    the sampled columns' targets need only their own columns of Wq and W_hat)."""
+    lut = oracle.code_lut("exl3_mul1")
+    picks = [np.unique(np.linspace(c0, c0 + nt - 1, min(nt, per_seg)).astype(int))
+             for c0, nt, _K in segs]
+    tiles = np.concatenate(picks)
+    cols = torch.from_numpy((tiles[:, None] * 16 + np.arange(16)[None, :]).reshape(-1))
+    Wq_h = Wq[:, cols.to(Wq.device)].cpu().numpy()
+    hat_h = hatW[:, cols.to(Wq.device)].cpu().numpy()
+    L_h = Lfac.cpu().numpy()
+    E = Wq_h - hat_h
+    for i in blocks:
+        Xr, A = oracle.ldlq_block_targets(Wq_h, L_h, hat_h, int(i), E)
+        Xi = X[i][torch.from_numpy(tiles).to(X.device)].cpu().numpy()
+        sti = st[i][torch.from_numpy(tiles).to(st.device)].cpu().numpy()
+        ratio = (np.abs(Xi.astype(np.float64) - Xr) / np.maximum(A, 1e-30)).max()
+        assert ratio <= 1e-5, f"k-block {i}: targets off by {ratio:.3g} of |terms|"
+        o = 0
+        for (c0, nt, K), pk in zip(segs, picks):
+            sl = slice(o, o + pk.size)
+            ref = oracle.tailbite(np.ascontiguousarray(Xi[sl]), lut, K, pivot=128, margin=0,
+                                  nthreads=NTH)
+            bad = np.nonzero((ref != sti[sl]).any(1))[0]
+            assert bad.size == 0, f"k-block {i}, K={K}: {bad.size} tiles differ, first {pk[bad[:5]]}"
+            o += pk.size
+
+
+def test_config5_layer_parity(tmp_path):
+    """Config 5, the 27B-shape mixed-K stack: layer 0 through the product
+    driver (exl3b.stack: q/k/v at K = 5, 7, 7 on one Hessian, o at 6,
+    gate/up at 5, 5, down at 4), written as EXL3 files.  Every group's
+    sweep is rerun here with its encoder targets exposed: the stored
+    trellises equal it bit for bit, and sampled k-blocks of every group
+    (first, middle and last) re-encoded by the CPU oracle from those targets
+    give the same states, at every member's K."""
+    from exl3b import export, stack, synth
+    from oracle import exl3_oracle as oracle
+    dev = torch.device("cuda", 0)
+    layer = 0
+    stack.quantize_layer(layer, dev, out_root=tmp_path)
+    for group, dim, members in synth.STACK_GROUPS:
+        H = synth.hessian(dim, synth.stack_hessian_seed(layer, group), dev)
+        Ws = [synth.stack_weight(layer, m, dev) for m in members]
+        Ks = [synth.SC5_K[m] for m in members]
+        suh, meta, Wq, Lfac, hatW, trl, st, X, widths = _prepare(Ws, H, Ks, dev)
+        for m, W, mt, t in zip(members, Ws, meta, trl):
+            f = export.load_quantized(tmp_path / "L00" /
+                                      f"{stack.MODULE_NAMES[m]}.safetensors")
+            assert torch.equal(f["trellis"], t.cpu()), (group, m)
+        _check_transform(oracle, Ws[0], suh, meta[0])
+        segs, c0 = [], 0
+        for w, K in zip(widths, Ks):
+            segs.append((c0, w // 16, K))
+            c0 += w // 16
+        tk = dim // 16
+        _check_sampled(oracle, [tk - 1, tk // 2, 0], segs, Wq, Lfac, hatW, st, X)
+        del H, Ws, Wq, Lfac, hatW, trl, st, X
+        torch.cuda.empty_cache()
