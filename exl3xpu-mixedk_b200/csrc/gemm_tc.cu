@@ -299,17 +299,29 @@ feedback_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 // R contiguous, row pitch ld) as hi / lo arrays [R][kp] (K contiguous, kp =
 // K rounded up to 32, zero padded), each value x (times `sign`) as
 // hi = tf32(x), lo = tf32(x - hi) -- the same split as split_row.  Then
-// gemm_tf32x3_kernel streams 128 x 32 boxes of the four arrays with TMA
-// (128-byte swizzle: the boxes land in the UMMA K-major canonical layout as
-// they are) through a kStages ring: thread 0 loads, thread 32 issues the
-// MMAs (lo.hi, hi.lo, hi.hi per 8-deep k step, as above) and commits each
-// stage back to the loader; all four warps run the same epilogue, which adds
-// sa * acc (sa = +-1: exact, and the same bits as splitting sa * A).
+// gemm_tf32x3_kernel: persistent, warp-specialised 3xTF32 GEMM over pre-split
+// operands.  One CTA per SM walks the 128 x 128 tiles of C (row-major tile
+// order, CTA b takes tiles b, b + grid, ...):
+//   * warp 0 (one thread) streams 128 x 32 boxes of the four arrays with TMA
+//     (128-byte swizzle: the boxes land in the UMMA K-major canonical layout
+//     as they are) through a kStages ring of full / empty mbarriers;
+//   * warp 1 (one thread) issues the MMAs (lo.hi, hi.lo, hi.hi per 8-deep k
+//     step, as above) into one of two 128-column TMEM accumulators, tile by
+//     tile in turn, and commits each stage back to the loader and each
+//     finished tile to the epilogue;
+//   * warps 2-5 (warp w reads TMEM lanes 32 (w mod 4) ..) run the epilogue,
+//     C += sa * acc (sa = +-1: exact, and the same bits as splitting sa * A),
+//     and hand the accumulator back -- so tile i's read-modify-write of C
+//     overlaps tile i+1's MMAs, and the TMEM allocation and pipeline fill are
+//     paid once per SM instead of once per tile.
+// Every wait is bounded; on a time-out the CTA records the error, stops
+// issuing, waits (bounded) for its outstanding copies and MMAs, frees its
+// tensor memory and returns.
 constexpr int kStages = 3;
 constexpr int kSplitK = 512;                        // K per pre-split piece
 constexpr int kOpBox = 128 * kTK * 4;               // one 128 x 32 tf32 tile: 16 KB
 constexpr int kStage2 = 4 * kOpBox;                 // Ah | Al | Bh | Bl
-constexpr int kGemm2Smem = kStages * kStage2 + 128 + 1024;
+constexpr int kGemm2Smem = kStages * kStage2 + 128 + 1024;   // ring | barriers | align
 
 __global__ void __launch_bounds__(256)
 tf32_split_kernel(const float* __restrict__ X, int ld, int K, int R, float sign,
@@ -333,7 +345,17 @@ tf32_split_kernel(const float* __restrict__ X, int ld, int K, int R, float sign,
     }
 }
 
-__global__ void __launch_bounds__(128, 1)
+constexpr int kGemmThreads = 192;                   // loader, MMA, 4 epilogue warps
+
+// 128 x 128 tile t of the row-major tile grid (tn tiles per row); false when
+// `lower` skips it (entirely above the diagonal)
+__device__ __forceinline__ bool gemm_tile(int t, int tn, int lower, int& m0, int& n0) {
+    m0 = (t / tn) * kTM;
+    n0 = (t % tn) * kTN;
+    return !(lower && n0 > m0 + kTM - 1);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
                    const __grid_constant__ CUtensorMap tmAl,
                    const __grid_constant__ CUtensorMap tmBh,
@@ -344,137 +366,180 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
     uint8_t* gsm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + kStages * kStage2);
     // bars[0..S): stage full (TMA);  bars[S..2S): stage empty (MMA commit);
-    // bars[2S]: all MMAs done
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+    // bars[2S], [2S+1]: accumulator a full (MMA commit);  bars[2S+2], [2S+3]:
+    // accumulator a empty (128 epilogue arrivals);  bars[2S+4]: all MMAs done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+    __shared__ int fail_s;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
-    if (lower && n0 > m0 + kTM - 1) return;
+    const int tm = (M + kTM - 1) / kTM, tn = (N + kTN - 1) / kTN;
+    const int ntiles = tm * tn;
     const uint32_t full0 = smem_u32(&bars[0]);
     const uint32_t empty0 = smem_u32(&bars[kStages]);
-    const uint32_t done = smem_u32(&bars[2 * kStages]);
+    const uint32_t afull0 = smem_u32(&bars[2 * kStages]);
+    const uint32_t aempty0 = smem_u32(&bars[2 * kStages + 2]);
+    const uint32_t done = smem_u32(&bars[2 * kStages + 4]);
     const int nchunks = kp / kTK;
     if (t == 0) {
-        for (int i = 0; i < 2 * kStages + 1; ++i)
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&bars[i])) : "memory");
+        for (int i = 0; i < 2 * kStages + 5; ++i) {
+            const uint32_t cnt = (i == 2 * kStages + 2 || i == 2 * kStages + 3) ? 128u : 1u;
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;"
+                         :: "r"(smem_u32(&bars[i])), "r"(cnt) : "memory");
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fail_s = 0;
     }
-    if (warp == 0) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_u32(tmem_slot)), "r"(kTN) : "memory");
+                     :: "r"(smem_u32(tmem_slot)), "r"(2 * kTN) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    __shared__ int fail_s;
-    if (t == 0) fail_s = 0;
-    __syncthreads();
 
     if (t == 0) {
-        // loader: chunk kc into stage kc % S once the MMAs of chunk kc - S are done
-        int issued = 0;
+        // loader: global chunk it into stage it % S once the MMAs of chunk it - S
+        // have read it
+        int it = 0, issued = 0;
         bool ok = true;
-        for (int kc = 0; kc < nchunks && ok; ++kc) {
-            const int s = kc % kStages, r = kc / kStages;
-            if (r > 0) ok = mbar_wait(empty0 + 8 * s, (r - 1) & 1);
-            if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
-            const uint32_t bar = full0 + 8 * s;
-            const uint32_t dst = smem_u32(gsm + s * kStage2);
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
-                         :: "r"(bar), "r"(kStage2) : "memory");
-            tma_load_2d(dst, &tmAh, kc * kTK, m0, bar);
-            tma_load_2d(dst + kOpBox, &tmAl, kc * kTK, m0, bar);
-            tma_load_2d(dst + 2 * kOpBox, &tmBh, kc * kTK, n0, bar);
-            tma_load_2d(dst + 3 * kOpBox, &tmBl, kc * kTK, n0, bar);
-            issued = kc + 1;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            int m0, n0;
+            if (!gemm_tile(tile, tn, lower, m0, n0)) continue;
+            for (int kc = 0; kc < nchunks; ++kc, ++it) {
+                const int s = it % kStages, r = it / kStages;
+                if (r > 0) ok = mbar_wait(empty0 + 8 * s, (r - 1) & 1);
+                if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
+                const uint32_t bar = full0 + 8 * s;
+                const uint32_t dst = smem_u32(gsm + s * kStage2);
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                             :: "r"(bar), "r"(kStage2) : "memory");
+                tma_load_2d(dst, &tmAh, kc * kTK, m0, bar);
+                tma_load_2d(dst + kOpBox, &tmAl, kc * kTK, m0, bar);
+                tma_load_2d(dst + 2 * kOpBox, &tmBh, kc * kTK, n0, bar);
+                tma_load_2d(dst + 3 * kOpBox, &tmBl, kc * kTK, n0, bar);
+                issued = it + 1;
+            }
         }
         if (!ok) {
             atomicExch(&fail_s, 1);
             // every issued load lands before the shared memory is released
-            for (int kc = 0; kc < issued; ++kc)
-                mbar_wait(full0 + 8 * (kc % kStages), (kc / kStages) & 1);
+            for (int i = 0; i < issued; ++i)
+                mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1);
         }
     } else if (t == 32) {
-        // MMA issuer
-        int committed = 0;
+        // MMA issuer: tile lt of this CTA into accumulator lt & 1
+        int it = 0, lt = 0;
         bool ok = true;
-        for (int kc = 0; kc < nchunks; ++kc) {
-            const int s = kc % kStages, r = kc / kStages;
-            ok = mbar_wait(full0 + 8 * s, r & 1);
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            int m0, n0;
+            if (!gemm_tile(tile, tn, lower, m0, n0)) continue;
+            const int a = lt & 1, u = lt >> 1;
+            if (u > 0) ok = mbar_wait(aempty0 + 8 * a, (u - 1) & 1);
             if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t aH = smem_u32(gsm + s * kStage2), aL = aH + kOpBox;
-            const uint32_t bH = aH + 2 * kOpBox, bL = aH + 3 * kOpBox;
+            const uint32_t acc = tmem + (uint32_t)(a * kTN);
+            for (int kc = 0; kc < nchunks; ++kc, ++it) {
+                const int s = it % kStages, r = it / kStages;
+                ok = mbar_wait(full0 + 8 * s, r & 1);
+                if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t aH = smem_u32(gsm + s * kStage2), aL = aH + kOpBox;
+                const uint32_t bH = aH + 2 * kOpBox, bL = aH + 3 * kOpBox;
 #pragma unroll
-            for (int kk = 0; kk < kTK / 8; ++kk) {
-                const uint32_t off = kk * 32;
-                umma_tf32(tmem, umma_desc_k_sw128(aL + off), umma_desc_k_sw128(bH + off),
-                          (kc > 0 || kk > 0) ? 1u : 0u);
-                umma_tf32(tmem, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bL + off), 1u);
-                umma_tf32(tmem, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bH + off), 1u);
+                for (int kk = 0; kk < kTK / 8; ++kk) {
+                    const uint32_t off = kk * 32;
+                    umma_tf32(acc, umma_desc_k_sw128(aL + off), umma_desc_k_sw128(bH + off),
+                              (kc > 0 || kk > 0) ? 1u : 0u);
+                    umma_tf32(acc, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bL + off), 1u);
+                    umma_tf32(acc, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bH + off), 1u);
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                             :: "r"(empty0 + 8 * s) : "memory");
             }
+            if (!ok) break;
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                         :: "r"(empty0 + 8 * s) : "memory");
-            committed = kc + 1;
+                         :: "r"(afull0 + 8 * a) : "memory");
+            ++lt;
         }
         if (!ok) atomicExch(&fail_s, 1);
         // the last commit tracks every earlier MMA of this thread
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                      :: "r"(done) : "memory");
-        (void)committed;
-    }
-    // everyone: all MMAs complete (or abandoned)
-    bool ok = mbar_wait(done, 0);
-    if (__syncthreads_or(!ok || fail_s)) {
-        if (t == 0) atomicCAS(err, 0, 4);
-    } else {
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int row = m0 + 32 * warp + lane;
+    } else if (warp >= 2) {
+        // epilogue: TMEM lanes 32 (warp mod 4) .. + 31 = rows of the tile
+        const int q = warp & 3;
         const bool vec = ((ldc & 3) == 0) && ((((uintptr_t)C) & 15) == 0);
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            int m0, n0;
+            if (!gemm_tile(tile, tn, lower, m0, n0)) continue;
+            const int a = lt & 1, u = lt >> 1;
+            bool ok = mbar_wait(afull0 + 8 * a, u & 1);
+            // one decision per warp: the TMEM loads below are warp-collective
+            ok = __all_sync(0xffffffffu, ok && !*(volatile int*)&fail_s);
+            if (!ok) {
+                if (lane == 0) atomicExch(&fail_s, 1);
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int row = m0 + 32 * q + lane;
 #pragma unroll 1
-        for (int cc = 0; cc < kTN / 32; ++cc) {
-            uint32_t r[32];
-            const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16) + 32 * cc;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-                "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
-                "[%32];"
-                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                  "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
-                  "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-                  "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-                  "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]),
-                  "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (row < M) {
-                float* crow = C + (size_t)row * ldc + n0 + 32 * cc;
-                const int lim = N - (n0 + 32 * cc);
-                if (vec && lim >= 32) {
+            for (int cc = 0; cc < kTN / 32; ++cc) {
+                uint32_t r[32];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * kTN + 32 * cc);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                    "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+                    "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+                    "[%32];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                      "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                      "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+                      "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                      "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]),
+                      "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (cc == kTN / 32 - 1) {
+                    // the accumulator is read out: hand it back to the MMA issuer
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];"
+                                 :: "r"(aempty0 + 8 * a) : "memory");
+                }
+                if (row < M) {
+                    float* crow = C + (size_t)row * ldc + n0 + 32 * cc;
+                    const int lim = N - (n0 + 32 * cc);
+                    if (vec && lim >= 32) {
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        float4 c4 = *reinterpret_cast<float4*>(crow + j);
-                        c4.x += sa * __uint_as_float(r[j]);
-                        c4.y += sa * __uint_as_float(r[j + 1]);
-                        c4.z += sa * __uint_as_float(r[j + 2]);
-                        c4.w += sa * __uint_as_float(r[j + 3]);
-                        *reinterpret_cast<float4*>(crow + j) = c4;
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 c4 = *reinterpret_cast<float4*>(crow + j);
+                            c4.x += sa * __uint_as_float(r[j]);
+                            c4.y += sa * __uint_as_float(r[j + 1]);
+                            c4.z += sa * __uint_as_float(r[j + 2]);
+                            c4.w += sa * __uint_as_float(r[j + 3]);
+                            *reinterpret_cast<float4*>(crow + j) = c4;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < lim) crow[j] = crow[j] + sa * __uint_as_float(r[j]);
                     }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < lim) crow[j] = crow[j] + sa * __uint_as_float(r[j]);
                 }
             }
+            ++lt;
         }
+    }
+    // everyone: all MMAs complete (or abandoned)
+    const bool ok = mbar_wait(done, 0);
+    if (__syncthreads_or(!ok || fail_s)) {
+        if (t == 0) atomicCAS(err, 0, 4);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0)
+    if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
-                     :: "r"(tmem), "r"(kTN) : "memory");
+                     :: "r"(tmem), "r"(2 * kTN) : "memory");
 }
 
 // ---------------------------------------------------------------- host side
@@ -580,9 +645,11 @@ int gemm_presplit_run(int M, int N, int kp, const float* Ah, const float* Al, co
     if (!rc) rc = encode_split(&tBh, Bh, kp, N);
     if (!rc) rc = encode_split(&tBl, Bl, kp, N);
     if (rc) return rc;
-    dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
-    gemm_tf32x3_kernel<<<grid, 128, kGemm2Smem, stream>>>(tAh, tAl, tBh, tBl, C, ldc, M, N, kp,
-                                                         sa, lower, err);
+    const int tiles = ((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
+    const int sms = device_sms();
+    const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);     // persistent CTAs
+    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemm2Smem, stream>>>(tAh, tAl, tBh, tBl, C, ldc,
+                                                                  M, N, kp, sa, lower, err);
     note_launch();
     return check_cuda(cudaGetLastError(), "gemm_tf32x3 launch") ? RC_DEVICE_ERROR : RC_OK;
 }
