@@ -56,12 +56,15 @@ def quantize_linear_columns(W: torch.Tensor, H_x: torch.Tensor | None, cols: tup
                             code: str = "exl3_mul1", K: int = 4, percdamp: float = 0.01,
                             su_seed: int = 20261011, buf_cols: int = 128,
                             use_ldlq: bool = True, device=None, margin: int = 0,
-                            pivot: int | None = None, out_device=None) -> dict:
+                            pivot: int | None = None, out_device=None,
+                            Lfac: torch.Tensor | None = None) -> dict:
     """Output channels [n0, n1) of quantize_linear(W [out, in], H_x, ...):
     the same dict with W_hat [n1 - n0, in], trellis [in/16, (n1 - n0)/16, 16K]
     and svh [n1 - n0] restricted to the range (suh and Wscale are the whole
     tensor's), plus "cols": (n0, n1).  Bit-identical to that slice of the
-    unsplit result."""
+    unsplit result.  Lfac: the damped block-LDL factor of H_x already
+    computed by lfac() (members of one fused module share it); H_x is then
+    not used."""
     api._check_code(code)
     api._check_K(K)
     m_out, k_in = W.shape
@@ -83,9 +86,10 @@ def quantize_linear_columns(W: torch.Tensor, H_x: torch.Tensor | None, cols: tup
     Wscale_d = api._rms_scale(parts, Wi.numel(), float(lut_rms), dev)
     Wq = api._div(Wi[:, n0:n1].contiguous(), Wscale_d)
     del Wi
-    Lfac = None
-    if use_ldlq and H_x is not None:
-        Lfac = api._damped_lfac(H_x, suh, percdamp, dev)
+    if not use_ldlq:
+        Lfac = None
+    elif Lfac is None and H_x is not None:
+        Lfac = lfac(H_x, k_in, percdamp, su_seed, dev)
     pv = api.STEPS // 2 if pivot is None else int(pivot)
     w = n1 - n0
     hatW, trl, _st, _ = api._sweep(Wq, Lfac, [K], [w], code, pv, margin, buf_cols)
@@ -107,6 +111,84 @@ def quantize_linear_columns(W: torch.Tensor, H_x: torch.Tensor | None, cols: tup
            "cols": (n0, n1)}
     api._out_done(dev, od)
     return out
+
+
+def quantize_columns_fused(pieces: list, Lfac: torch.Tensor | None, code: str = "exl3_mul1",
+                           su_seed: int = 20261011, buf_cols: int = 128, device=None,
+                           margin: int = 0, pivot: int | None = None, out_device=None) -> list:
+    """Output-channel ranges of the members of one fused module (one shared
+    input Gram, so one Lfac), quantized in ONE sweep with a column segment per
+    piece at its own K: pieces = [(W_j [out_j, in], (n0, n1), K_j), ...].
+    Returns one quantize_linear_columns dict per piece, bit-identical to it
+    (columns never interact); a single sweep keeps narrow pieces (k / v, the
+    ends of a rank's range) on a full-width launch."""
+    if not pieces:
+        return []
+    code = code or "exl3_mul1"
+    api._check_code(code)
+    k_in = pieces[0][0].shape[1]
+    dev = api._cuda_device(device if device is not None else pieces[0][0].device)
+    api._select(dev)
+    s = api._stream(dev)
+    lut_rms = api._lut_rms(api.get_lut(code))
+    suh = api.sign_vec(k_in, su_seed).half()
+    prep = []
+    for W, cols, K in pieces:
+        api._check_K(K)
+        m_out = W.shape[0]
+        n0, n1 = int(cols[0]), int(cols[1])
+        if W.shape[1] != k_in or not (0 <= n0 < n1 <= m_out) or n0 % ALIGN or n1 % ALIGN:
+            raise ValueError(f"piece [{n0}, {n1}) of W {tuple(W.shape)} (in = {k_in}): need "
+                             "128-aligned ranges of members with one input dim")
+        svh = api.sign_vec(m_out, su_seed + 1).half()
+        W_dev = W.detach().to(dev, non_blocking=True)
+        if W_dev.dtype not in api.DTYPE_IDS:
+            W_dev = W_dev.float()
+        Wi, parts = api._encode_inner(W_dev.contiguous(), suh, svh, dev)
+        del W_dev
+        Wscale_d = api._rms_scale(parts, Wi.numel(), float(lut_rms), dev)
+        prep.append((api._div(Wi[:, n0:n1].contiguous(), Wscale_d), Wscale_d, svh, n0, n1, K))
+        del Wi
+    Wq = prep[0][0] if len(prep) == 1 else torch.cat([p[0] for p in prep], dim=1)
+    widths = [p[4] - p[3] for p in prep]
+    pv = api.STEPS // 2 if pivot is None else int(pivot)
+    hatW, trl, _st, _ = api._sweep(Wq, Lfac, [p[5] for p in prep], widths, code, pv, margin,
+                                   buf_cols)
+    del Wq
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    su32 = suh.float().to(dev)
+    outs_dev, c0 = [], 0
+    for (_wq, Wscale_d, svh, n0, n1, K), t, w in zip(prep, trl, widths):
+        hw = hatW[:, c0:c0 + w]
+        api._verify_async(t, hw, K, code, bad)
+        sv32 = svh[n0:n1].float().to(dev).contiguous()
+        W_hat = torch.empty(w, k_in, dtype=torch.float32, device=dev)
+        call("exl3b_incoherence_inv", hw.contiguous().data_ptr(), k_in, w,
+             Wscale_d.data_ptr(), su32.data_ptr(), sv32.data_ptr(), W_hat.data_ptr(), s)
+        outs_dev.append((W_hat, t))
+        c0 += w
+    od = torch.device(out_device) if out_device is not None else dev
+    wscales = torch.cat([p[1] for p in prep]).tolist()
+    api._verify_raise(bad, "quantize_columns_fused")
+    outs = []
+    for (_wq, _sc, svh, n0, n1, K), (W_hat, t), wscale in zip(prep, outs_dev, wscales):
+        outs.append({"W_hat": api._out(W_hat, od), "trellis": api._out(t, od),
+                     "suh": api._out(suh, od), "svh": api._out(svh[n0:n1].contiguous(), od),
+                     "Wscale": float(wscale), "lut_rms": float(lut_rms), "code": code,
+                     "K": int(K), "L": 16, "V": 1, "use_ldlq": Lfac is not None,
+                     "channel_scales": False, "cols": (n0, n1)})
+    api._out_done(dev, od)
+    return outs
+
+
+def lfac(H_x: torch.Tensor, k_in: int, percdamp: float = 0.01, su_seed: int = 20261011,
+         device=None) -> torch.Tensor:
+    """The damped block-LDL factor quantize_linear computes from H_x (the
+    same rotation by the su sign vector of `su_seed`, damping and fallback)."""
+    dev = api._cuda_device(device if device is not None else H_x.device)
+    api._select(dev)
+    suh = api.sign_vec(k_in, su_seed).half()
+    return api._damped_lfac(H_x, suh, percdamp, dev)
 
 
 def gather_columns(part: dict, n: int, group=None) -> dict:

@@ -159,6 +159,117 @@ def quantize_layer(layer: int, device, Ks: dict | None = None, out_root=None,
     return stats
 
 
+ALIGN = 128
+
+
+def layer_ranges(world: int) -> list:
+    """Per rank, the (tensor, n0, n1) output-channel ranges of one layer of
+    the stack when the layer itself is split over `world` ranks: the layer's
+    tensors in order (synth.STACK_SHAPES) form one sequence of 128-channel
+    chunks, a chunk of tensor m weighing 128 x in_m weights (the work per
+    weight does not depend on K), cut into `world` contiguous parts of
+    near-equal weight.  Every channel belongs to exactly one rank, a rank's
+    channels of one tensor form one range, and ranks hold increasing ranges."""
+    from . import synth
+    if world < 1:
+        raise ValueError("world >= 1")
+    chunks = [(name, n0, ALIGN * in_f) for name, out_f, in_f in synth.STACK_SHAPES
+              for n0 in range(0, out_f, ALIGN)]
+    total = sum(c[2] for c in chunks)
+    parts = [[] for _ in range(world)]
+    acc = 0
+    for name, n0, mass in chunks:
+        r = min(world - 1, int((2 * acc + mass) * world // (2 * total)))
+        acc += mass
+        parts[r].append((name, n0))
+    out = []
+    for part in parts:
+        ranges = []
+        for name, n0 in part:
+            if ranges and ranges[-1][0] == name and ranges[-1][2] == n0:
+                ranges[-1] = (name, ranges[-1][1], n0 + ALIGN)
+            else:
+                ranges.append((name, n0, n0 + ALIGN))
+        out.append(ranges)
+    return out
+
+
+def quantize_layer_split(layer: int, device, group=None, Ks: dict | None = None,
+                         writer: Writer | None = None, out_root=None,
+                         hessian_dir=None) -> list:
+    """One layer of the stack with its output channels spread over the ranks
+    of `group` (layer_ranges; a single process is a world of one).  Each rank
+    factors the Hessian of every input group it touches once, quantizes its
+    channel ranges of each group in one sweep (exl3b.shard.
+    quantize_columns_fused: bit-identical to the same channels of the
+    unsplit tensors, self-checked), and the finished
+    trellises and scales are all-gathered (NCCL).  Rank 0 assembles each
+    tensor and writes its EXL3 files; returns its per-tensor stats there, []
+    on the other ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from . import api, export, shard, synth
+    Ks = dict(synth.SC5_K if Ks is None else Ks)
+    split = dist.is_available() and dist.is_initialized()
+    rank = dist.get_rank(group) if split else 0
+    world = dist.get_world_size(group) if split else 1
+    plan = layer_ranges(world)
+    mine = plan[rank]
+    parts = {}
+    for gname, dim, members in synth.STACK_GROUPS:
+        todo = [(m, a, b) for m, a, b in mine if m in members]
+        if not todo:
+            continue
+        if hessian_dir is not None:
+            H = load_hessian(hessian_path(hessian_dir, layer, gname, members), dim, device)
+        else:
+            H = synth.hessian(dim, synth.stack_hessian_seed(layer, gname), device)
+        L = shard.lfac(H, dim, device=device)
+        del H
+        pieces = [(synth.stack_weight(layer, m, device), (a, b), Ks[m]) for m, a, b in todo]
+        for (m, _a, _b), r in zip(todo, shard.quantize_columns_fused(pieces, L,
+                                                                     out_device=device)):
+            parts[m] = r
+        del L, pieces
+    stats = []
+    for name, out_f, in_f in synth.STACK_SHAPES:
+        K = Ks[name]
+        widths = [sum(b - a for m, a, b in rr if m == name) for rr in plan]
+        p = parts.get(name)
+        if world > 1:
+            wmax = max(widths)
+            buf = torch.zeros(in_f // 16, wmax // 16, 16 * K, dtype=torch.int16, device=device)
+            if p is not None:
+                buf[:, :p["trellis"].shape[1]] = p["trellis"]
+            # collectives have no int16 type: the trellis travels as its bytes
+            got = [torch.empty_like(buf.view(torch.uint8)) for _ in range(world)]
+            dist.all_gather(got, buf.view(torch.uint8), group=group)
+            sc = torch.tensor([p["Wscale"] if p is not None else 0.0], dtype=torch.float64,
+                              device=device)
+            scs = [torch.empty_like(sc) for _ in range(world)]
+            dist.all_gather(scs, sc, group=group)
+            if rank != 0:
+                continue
+            trellis = torch.cat([g.view(torch.int16)[:, :w // 16]
+                                 for g, w in zip(got, widths) if w], dim=1)
+            wscale = float(next(float(x.item()) for x, w in zip(scs, widths) if w))
+        else:
+            trellis, wscale = p["trellis"], p["Wscale"]
+        res = {"trellis": trellis, "suh": api.sign_vec(in_f, 20261011).half(),
+               "svh": api.sign_vec(out_f, 20261012).half(), "Wscale": wscale, "K": K,
+               "code": "exl3_mul1", "channel_scales": False}
+        meta = {"group": next(g for g, _d, ms in synth.STACK_GROUPS if name in ms),
+                "layer": layer, "split_ranks": world}
+        if writer is not None:
+            writer.submit(layer, MODULE_NAMES[name], res, meta)
+        elif out_root is not None:
+            export.save_quantized(out_root, layer, MODULE_NAMES[name], res, meta=meta)
+        stats.append({"layer": layer, "tensor": name, "K": K, "weights": out_f * in_f,
+                      "Wscale": wscale})
+    return stats
+
+
 def run_rank(n_layers: int, rank: int, world: int, device, out_root=None,
              quantize=quantize_layer, **kw) -> list:
     """This rank's share of the stack; `quantize(layer, device, ...)` returns
@@ -174,6 +285,9 @@ def main(argv=None) -> int:
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--out", default=None, help="EXL3 per-tensor output root (optional)")
     ap.add_argument("--tensors", default=None, help="comma list of tensors (default all)")
+    ap.add_argument("--split-layers", action="store_true",
+                    help="split every layer over all ranks (per-layer latency) instead of "
+                         "whole layers per rank")
     ap.add_argument("--hessians", default=None,
                     help="directory of captured input Grams (L{layer}_{module}.safetensors, "
                          "key H); default: seeded synthetic Hessians")
@@ -195,8 +309,19 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
     writer = Writer(a.out) if a.out else None
     ev0.record()
-    stats = run_rank(a.layers, rank, world, dev, a.out, tensors=tensors, writer=writer,
-                     hessian_dir=a.hessians)
+    if a.split_layers:
+        if tensors is not None:
+            raise SystemExit("--split-layers quantizes whole layers (no --tensors)")
+        stats = []
+        for layer in range(a.layers):
+            stats.extend(quantize_layer_split(layer, dev, writer=writer if rank == 0 else None,
+                                              hessian_dir=a.hessians))
+        for st in stats:
+            st.setdefault("seconds", 0.0)
+            st.setdefault("synth_seconds", 0.0)
+    else:
+        stats = run_rank(a.layers, rank, world, dev, a.out, tensors=tensors, writer=writer,
+                         hessian_dir=a.hessians)
     if writer is not None:
         writer.close()          # the rank's last files are on disk inside the timing
     ev1.record()
@@ -217,6 +342,9 @@ def main(argv=None) -> int:
                           "weights_per_s": weights / (float(ms.item()) / 1e3),
                           "quantize_gpu_seconds_all_ranks": q_s,
                           "input_synthesis_gpu_seconds_all_ranks": syn_s,
+                          "seconds_per_layer": float(ms.item()) / 1e3 / max(a.layers, 1),
+                          "sharding": "each layer split over all ranks" if a.split_layers
+                                      else "whole layers per rank",
                           "hessians": a.hessians or "synthetic"}))
     return 0
 

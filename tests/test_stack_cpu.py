@@ -114,3 +114,105 @@ def test_hessian_files_in_the_reference_naming(tmp_path):
     assert torch.equal(stack.load_hessian(p, 8, "cpu"), torch.eye(8))
     with pytest.raises(ValueError):
         stack.load_hessian(p, 16, "cpu")
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 7, 8])
+def test_layer_ranges_partition(world):
+    """Splitting one layer over `world` ranks: every output channel of every
+    tensor on exactly one rank, one range per (rank, tensor), ranges
+    increasing with the rank, and each rank's weight within one chunk of the
+    ideal share."""
+    plan = stack.layer_ranges(world)
+    assert len(plan) == world
+    total = sum(o * i for _n, o, i in synth.STACK_SHAPES)
+    biggest = max(stack.ALIGN * i for _n, _o, i in synth.STACK_SHAPES)
+    for name, out_f, in_f in synth.STACK_SHAPES:
+        got = sorted((a, b, r) for r, rr in enumerate(plan) for m, a, b in rr if m == name)
+        assert got[0][0] == 0 and got[-1][1] == out_f
+        for (a0, b0, r0), (a1, b1, r1) in zip(got, got[1:]):
+            assert b0 == a1 and r1 > r0            # contiguous, one range per rank
+        assert all(a % stack.ALIGN == 0 and b % stack.ALIGN == 0 for a, b, _ in got)
+    ins = {n: i for n, _o, i in synth.STACK_SHAPES}
+    for rr in plan:
+        mass = sum((b - a) * ins[m] for m, a, b in rr)
+        assert abs(mass - total / world) <= biggest, (mass, total / world)
+
+
+# a small stand-in layer for the gloo run of the split layer's gather
+_SMALL_SHAPES = [("q", 384, 256), ("k", 128, 256), ("v", 128, 256), ("o", 256, 384),
+                 ("gate", 512, 256), ("up", 512, 256), ("down", 256, 512)]
+_SMALL_GROUPS = [("attn", 256, ["q", "k", "v"]), ("o", 384, ["o"]),
+                 ("mlp", 256, ["gate", "up"]), ("down", 512, ["down"])]
+
+
+def _tile_code(name, in_f, n0, n1, K):
+    """Deterministic stand-in trellis of channels [n0, n1) of `name`."""
+    import torch
+    idx = [n for n, _o, _i in _SMALL_SHAPES].index(name)
+    tk, cols = in_f // 16, torch.arange(n0 // 16, n1 // 16)
+    t = (torch.arange(tk)[:, None, None] * 7 + cols[None, :, None] * 131
+         + torch.arange(16 * K)[None, None, :] + 1000 * idx)
+    return (t % 30000).to(torch.int16)
+
+
+def _split_rank_main(rank, world, port, out, q):
+    import torch
+    import torch.distributed as dist
+    from exl3b import shard
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    synth.STACK_SHAPES[:] = _SMALL_SHAPES
+    synth.STACK_GROUPS[:] = _SMALL_GROUPS
+    seen = []
+
+    def fake_fused(pieces, Lfac, out_device=None, **kw):
+        out = []
+        for (name, in_f), cols, K in pieces:
+            seen.append((name, cols))
+            out.append({"trellis": _tile_code(name, in_f, cols[0], cols[1], K),
+                        "Wscale": 0.5 + [n for n, _o, _i in _SMALL_SHAPES].index(name)})
+        return out
+
+    shard.quantize_columns_fused = fake_fused
+    shard.lfac = lambda H, k, **kw: None
+    synth.hessian = lambda dim, seed, device: None
+    synth.stack_weight = lambda layer, m, device: (m, {n: i for n, _o, i in _SMALL_SHAPES}[m])
+    stats = stack.quantize_layer_split(3, "cpu", out_root=out if rank == 0 else None)
+    dist.destroy_process_group()
+    q.put((rank, seen, stats))
+
+
+def test_two_rank_gloo_layer_split_assembles_every_tensor(tmp_path):
+    """A layer split over two gloo ranks (a small stand-in layer, the per-range
+    quantizer replaced by a deterministic code): each rank quantizes only its
+    planned ranges, and rank 0 writes every tensor whole, its trellis the
+    ranks' pieces side by side and its scale the tensor's."""
+    from exl3b import export
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_split_rank_main, args=(r, world, port, str(tmp_path), q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict((r, (seen, st)) for r, seen, st in (q.get(timeout=180) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    orig_shapes = list(synth.STACK_SHAPES)
+    synth.STACK_SHAPES[:] = _SMALL_SHAPES
+    try:
+        plan = stack.layer_ranges(world)
+    finally:
+        synth.STACK_SHAPES[:] = orig_shapes
+    for r in range(world):
+        assert sorted(got[r][0]) == sorted((m, (a, b)) for m, a, b in plan[r])
+    assert got[1][1] == [] and len(got[0][1]) == len(_SMALL_SHAPES)
+    for idx, (name, out_f, in_f) in enumerate(_SMALL_SHAPES):
+        f = export.load_quantized(tmp_path / "L03" / f"{stack.MODULE_NAMES[name]}.safetensors")
+        K = synth.SC5_K[name]
+        assert f["trellis"].shape == (in_f // 16, out_f // 16, 16 * K)
+        assert (f["trellis"] == _tile_code(name, in_f, 0, out_f, K)).all()
+        assert f["meta"]["Wscale"] == 0.5 + idx and f["meta"]["split_ranks"] == world

@@ -71,3 +71,21 @@ def test_harness_inputs_through_quantize():
     inner_ref = api.to_inner(ref["W_hat"].t(), ref["suh"].float(), ref["svh"].float())
     e_r = float((inner_ref.t() - Wt).square().sum() / Wt.square().sum())
     assert abs(e_h - e_r) <= 0.02 * e_r, (e_h, e_r)
+
+
+def test_layer_split_one_rank_matches_layer_driver(tmp_path):
+    """quantize_layer_split in a single process (a world of one: every
+    tensor whole, through the column-range path with one LDL factor per
+    input group) writes the same EXL3 fields as quantize_layer's fused
+    modules, for a full layer of the stack at its mixed K."""
+    from exl3b import export, stack, synth
+    dev = torch.device("cuda", 0)
+    stack.quantize_layer(0, dev, out_root=tmp_path / "a")
+    stats = stack.quantize_layer_split(0, dev, out_root=tmp_path / "b")
+    assert [s["tensor"] for s in stats] == [n for n, _o, _i in synth.STACK_SHAPES]
+    for name, _o, _i in synth.STACK_SHAPES:
+        a = export.load_quantized(tmp_path / "a" / "L00" / f"{stack.MODULE_NAMES[name]}.safetensors")
+        b = export.load_quantized(tmp_path / "b" / "L00" / f"{stack.MODULE_NAMES[name]}.safetensors")
+        for key in ("trellis", "suh", "svh"):
+            assert torch.equal(a[key], b[key]), (name, key)
+        assert a["meta"]["K"] == b["meta"]["K"] == synth.SC5_K[name]
