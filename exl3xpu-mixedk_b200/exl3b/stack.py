@@ -162,24 +162,53 @@ def quantize_layer(layer: int, device, Ks: dict | None = None, out_root=None,
 ALIGN = 128
 
 
-def layer_ranges(world: int) -> list:
-    """Per rank, the (tensor, n0, n1) output-channel ranges of one layer of
-    the stack when the layer itself is split over `world` ranks: the layer's
-    tensors in order (synth.STACK_SHAPES) form one sequence of 128-channel
-    chunks, a chunk of tensor m weighing 128 x in_m weights (the work per
-    weight does not depend on K), cut into `world` contiguous parts of
-    near-equal weight.  Every channel belongs to exactly one rank, a rank's
-    channels of one tensor form one range, and ranks hold increasing ranges."""
+# Time model of one rank's share of a split layer (ms), used only to choose
+# between candidate cuts.  A group's sweep over `cols` column tiles and tk
+# k-blocks takes about max(tk x CHAIN_MS, tk x cols / TILES_PER_MS): a column's
+# k-blocks are sequential, and a tile alone on an SM (fewer columns than tile
+# slots) takes ~1 ms, while a full-width sweep retires ~278 tiles per ms on
+# 148 SMs (config 2: 102400 tiles in 368 ms).  Plus the group's Hessian
+# synthesis and block LDL (~31 ms at in = 17408, ~7 ms below).
+CHAIN_MS = 1.0
+TILES_PER_MS = 278.0
+
+
+def _rank_ms(ranges) -> float:
     from . import synth
-    if world < 1:
-        raise ValueError("world >= 1")
+    ins = {n: i for n, _o, i in synth.STACK_SHAPES}
+    group = {m: g for g, _d, ms in synth.STACK_GROUPS for m in ms}
+    cols = {}
+    for m, a, b in ranges:
+        g = group[m]
+        cols[g] = (cols.get(g, (0, ins[m]))[0] + (b - a) // 16, ins[m])
+    return sum(max(k // 16 * CHAIN_MS, k // 16 * c / TILES_PER_MS) + (31 if k >= 16384 else 7)
+               for c, k in cols.values())
+
+
+def _cut_plan(world: int, snap: float) -> list:
+    from . import synth
     chunks = [(name, n0, ALIGN * in_f) for name, out_f, in_f in synth.STACK_SHAPES
               for n0 in range(0, out_f, ALIGN)]
     total = sum(c[2] for c in chunks)
+    share = total / world
+    bounds, acc = [0], 0
+    for _name, out_f, in_f in synth.STACK_SHAPES:
+        acc += out_f * in_f
+        bounds.append(acc)
+    cuts = []
+    for r in range(1, world):
+        c = r * share
+        for lo, hi in zip(bounds, bounds[1:]):
+            if lo < c < hi:
+                if c - lo < snap * share:
+                    c = lo
+                elif hi - c < snap * share:
+                    c = hi
+        cuts.append(c)
     parts = [[] for _ in range(world)]
     acc = 0
     for name, n0, mass in chunks:
-        r = min(world - 1, int((2 * acc + mass) * world // (2 * total)))
+        r = sum(1 for c in cuts if acc + mass / 2 > c)
         acc += mass
         parts[r].append((name, n0))
     out = []
@@ -192,6 +221,30 @@ def layer_ranges(world: int) -> list:
                 ranges.append((name, n0, n0 + ALIGN))
         out.append(ranges)
     return out
+
+
+def layer_ranges(world: int) -> list:
+    """Per rank, the (tensor, n0, n1) output-channel ranges of one layer of
+    the stack when the layer itself is split over `world` ranks.  The layer's
+    tensors in order (synth.STACK_SHAPES) form one sequence of 128-channel
+    chunks, a chunk of tensor m weighing 128 x in_m weights (the work per
+    weight does not depend on K), cut into `world` contiguous parts: at equal
+    weight, or with each cut moved to the nearest tensor boundary when it
+    would leave a piece smaller than a fraction of the share (a narrow piece
+    costs its whole chain of k-blocks: the down projection's 1088 take ~1 s
+    at any width).  Of the candidate cuts the one with the least predicted
+    time of the slowest rank is taken (_rank_ms).  Every channel belongs to
+    exactly one rank, a rank's channels of one tensor form one range, and
+    ranks hold increasing ranges (a rank may hold none)."""
+    if world < 1:
+        raise ValueError("world >= 1")
+    best = None
+    for snap in (0.0, 0.15, 0.3, 0.5):
+        plan = _cut_plan(world, snap)
+        cost = max(_rank_ms(rr) for rr in plan)
+        if best is None or cost < best[0]:
+            best = (cost, plan)
+    return best[1]
 
 
 def quantize_layer_split(layer: int, device, group=None, Ks: dict | None = None,

@@ -120,22 +120,35 @@ def test_hessian_files_in_the_reference_naming(tmp_path):
 def test_layer_ranges_partition(world):
     """Splitting one layer over `world` ranks: every output channel of every
     tensor on exactly one rank, one range per (rank, tensor), ranges
-    increasing with the rank, and each rank's weight within one chunk of the
-    ideal share."""
+    increasing with the rank, 128-aligned; the chosen cut never predicts a
+    slower slowest rank than the plain equal-weight cut, and an equal-weight
+    cut keeps each rank within one chunk of the ideal share."""
     plan = stack.layer_ranges(world)
     assert len(plan) == world
-    total = sum(o * i for _n, o, i in synth.STACK_SHAPES)
-    biggest = max(stack.ALIGN * i for _n, _o, i in synth.STACK_SHAPES)
     for name, out_f, in_f in synth.STACK_SHAPES:
         got = sorted((a, b, r) for r, rr in enumerate(plan) for m, a, b in rr if m == name)
         assert got[0][0] == 0 and got[-1][1] == out_f
         for (a0, b0, r0), (a1, b1, r1) in zip(got, got[1:]):
             assert b0 == a1 and r1 > r0            # contiguous, one range per rank
         assert all(a % stack.ALIGN == 0 and b % stack.ALIGN == 0 for a, b, _ in got)
+    even = stack._cut_plan(world, 0.0)
+    assert max(stack._rank_ms(rr) for rr in plan) <= max(stack._rank_ms(rr) for rr in even)
+    total = sum(o * i for _n, o, i in synth.STACK_SHAPES)
+    biggest = max(stack.ALIGN * i for _n, _o, i in synth.STACK_SHAPES)
     ins = {n: i for n, _o, i in synth.STACK_SHAPES}
-    for rr in plan:
+    for rr in even:
         mass = sum((b - a) * ins[m] for m, a, b in rr)
         assert abs(mass - total / world) <= biggest, (mass, total / world)
+
+
+def test_layer_ranges_avoid_narrow_long_chains():
+    """At 4 and 8 ranks no rank holds a narrow remnant of the down projection
+    (1088 sequential k-blocks) on top of other work."""
+    for world in (4, 8):
+        for rr in stack.layer_ranges(world):
+            downs = [(a, b) for m, a, b in rr if m == "down"]
+            if downs and len(rr) > 1:
+                assert all(b - a >= 1024 for a, b in downs), rr
 
 
 # a small stand-in layer for the gloo run of the split layer's gather
