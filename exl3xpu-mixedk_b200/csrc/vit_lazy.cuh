@@ -78,7 +78,7 @@ struct Lazy {
     // half-row rebuild: (w, w') candidate pairs, per lane, lanes per w
     static constexpr int PAIRS = G::NC * G::NC;
     static constexpr int CPL = PAIRS > 32 ? PAIRS / 32 : 1;
-    static constexpr int GL = PAIRS > 32 ? 32 / G::NC : G::NC;
+    static constexpr int GL = PAIRS <= 32 ? G::NC : (G::NC < 32 ? 32 / G::NC : 1);
     // the ring of best arrays (64 KB: K = 2: 2, K = 3: 2, K = 4: 4; two when
     // the threads store the rows) and the rows per bulk copy (half the ring,
     // aligned: a batch's arrays are adjacent)
