@@ -17,7 +17,10 @@ mul1, quantize_linear defaults: pivot 128, margin 0), packing and W_hat.
           rank, no collective on the data path): weak scaling -- the layer-
           sharded way a stack of projections runs.  "per_layer" adds the time
           of ONE projection with its output columns split over the N ranks
-          (exl3b.shard; all-gather of the finished tensors included)
+          (exl3b.shard; all-gather of the finished tensors included);
+          "per_layer_c5" the time of one 27B-shape layer (config 5 shapes and
+          mixed K) with its output channels split over the N ranks
+          (exl3b.stack.quantize_layer_split), at every N including 1
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config c2|c3|c4] [--K k]
@@ -286,6 +289,40 @@ def _split_leg(args, dev, world, local, rank, barrier):
             "column_tiles_per_rank": [(b - a) // 16 for a, b in cols]}
 
 
+def _layer_leg(args, dev, world, barrier):
+    """Per-layer time of one 27B-shape layer (config 5: q/k/v, o, gate/up,
+    down at the SC5 mixed K = 4..7, seeded synthetic weights and Hessians)
+    split over the N ranks (exl3b.stack.quantize_layer_split: channel ranges
+    chosen by a per-rank time model, NCCL all-gather of the trellises inside
+    the timed region; N = 1: the whole layer on one GPU).  One warm-up layer,
+    then layers 1 .. L timed with CUDA events, max over ranks.  Weight and
+    Hessian synthesis are inside the time, as they are for the stack driver."""
+    import torch
+    import torch.distributed as dist
+    from exl3b import stack, synth
+    if args.config != "c2" or args.dim != DIM or args.no_layer:
+        return None
+    nl = max(1, min(args.steps, 2))
+    stack.quantize_layer_split(0, dev)
+    barrier()
+    s = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for layer in range(1, nl + 1):
+        stack.quantize_layer_split(layer, dev)
+    e1.record(s)
+    barrier()
+    ms = torch.tensor([e0.elapsed_time(e1) / nl], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    return {"layer": "27B-shape layer (config 5 shapes, SC5 K: q5 k7 v7 o6 gate5 up5 down4)",
+            "split": f"output channels over {world} rank(s), time-model cuts, NCCL all-gather",
+            "n_gpus": world, "layers_timed": nl, "seconds_per_layer": ms / 1e3,
+            "weights_per_s": synth.stack_weights_per_layer() / (ms / 1e3)}
+
+
 def _to_host(inp):
     if isinstance(inp, list):
         return [_to_host(x) for x in inp]
@@ -378,6 +415,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-layer", action="store_true",
+                    help="skip the per-layer leg of one config-5 layer split over the ranks")
     ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4"],
                     help="workload: c2 (default bench line), c3 fused mixed-K qkv, c4 at --K")
     ap.add_argument("--K", type=int, default=4, help="bits per weight for --config c4")
@@ -447,6 +486,7 @@ def main():
     # per-layer time with one projection split over the ranks (N = 1: the
     # step itself, one whole projection on one GPU)
     per_layer = _split_leg(args, dev, world, local, rank, barrier) if world > 1 else None
+    layer_c5 = _layer_leg(args, dev, world, barrier)
 
     # ---- e2e: public API from pinned host buffers, copies inside the step
     ms_e2e = float("nan")
@@ -533,6 +573,8 @@ def main():
             "split": "none: one whole projection per GPU (N = 1, or a fused module)",
             "n_gpus": world, "ms_per_layer": ms, "weights_per_s": weights / (ms / 1e3)},
     }
+    if layer_c5 is not None:
+        line["per_layer_c5"] = layer_c5
     if world > 1:
         dist.barrier(device_ids=[local])
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.dim == DIM
