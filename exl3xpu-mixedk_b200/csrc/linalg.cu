@@ -182,10 +182,21 @@ potrf_inv_kernel(float* __restrict__ A, int n, int j0, int nb, int* __restrict__
     __shared__ int bad_s;
     if (*status) return;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    for (int idx = t; idx < kNB * kNB; idx += 512) {
-        const int r = idx / kNB, c = idx % kNB;
-        S[r][c] = (r < nb && c <= r) ? A[(size_t)(j0 + r) * n + (j0 + c)] : 0.0f;
-        V[r][c] = 0.0f;
+    {
+        // all eight loads of a thread in flight at once (the block is one
+        // dependent step of the factorisation's serial chain)
+        float v[kNB * kNB / 512];
+#pragma unroll
+        for (int q = 0; q < kNB * kNB / 512; ++q) {
+            const int idx = t + 512 * q, r = idx / kNB, c = idx % kNB;
+            v[q] = (r < nb && c <= r) ? A[(size_t)(j0 + r) * n + (j0 + c)] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < kNB * kNB / 512; ++q) {
+            const int idx = t + 512 * q, r = idx / kNB, c = idx % kNB;
+            S[r][c] = v[q];
+            V[r][c] = 0.0f;
+        }
     }
     if (t == 0) bad_s = 0;
     __syncthreads();
@@ -195,6 +206,7 @@ potrf_inv_kernel(float* __restrict__ A, int n, int j0, int nb, int* __restrict__
         if (warp == 0) {
             // lane l < 16 holds row l of the 16 x 16 diagonal block in registers
             float a[16];
+            float rdg[16];                           // 1 / L[j][j], the same in every lane
 #pragma unroll
             for (int m = 0; m < 16; ++m) a[m] = (lane < 16) ? S[k0 + lane][k0 + m] : 0.0f;
             int badj = -1;                           // the same in every lane
@@ -203,9 +215,14 @@ potrf_inv_kernel(float* __restrict__ A, int n, int j0, int nb, int* __restrict__
                 const float d = __shfl_sync(0xffffffffu, a[j], j);
                 const bool good = (d > 0.0f) && isfinite(d);
                 if (!good && badj < 0) badj = j;
-                const float djj = sqrtf(good ? d : 1.0f);
-                if (lane == j) a[j] = djj;
-                if (lane > j) a[j] = a[j] / djj;
+                // 1 / sqrt(d) once per column, warp-uniform (one MUFU operation,
+                // ~2 ulp), then multiplies: the per-lane IEEE divisions were the
+                // serial chain's longest links.  The factor is needed to fp32
+                // accuracy, not to the last bit.
+                const float dd = good ? d : 1.0f;
+                rdg[j] = rsqrtf(dd);
+                const float djj = dd * rdg[j];
+                a[j] = (lane == j) ? djj : (lane > j ? a[j] * rdg[j] : a[j]);
                 // rank-1 update: a[c] -= a[j] * L[c][j] for j < c <= lane
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
@@ -225,9 +242,7 @@ potrf_inv_kernel(float* __restrict__ A, int n, int j0, int nb, int* __restrict__
                 __syncwarp();
                 if (lane < 16) {     // column `lane` of the block's inverse
                     const int c = lane;
-                    float rd[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) rd[j] = 1.0f / S[k0 + j][k0 + j];
+                    const float (&rd)[16] = rdg;
                     float x[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
