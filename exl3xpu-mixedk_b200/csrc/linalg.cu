@@ -337,10 +337,23 @@ panel_apply_kernel(float* __restrict__ A, int n, int j0, int nb,
     const int t = threadIdx.x;
     const int rest = n - j0 - nb;
     const int r0 = blockIdx.x * kNB;
-    for (int idx = t; idx < kNB * kNB; idx += 256) {
-        const int r = idx / kNB, c = idx % kNB;
-        LI[r][c] = (r < nb && c < nb) ? Linv[idx] : 0.0f;
-        B[r][c] = (r0 + r < rest && c < nb) ? A[(size_t)(j0 + nb + r0 + r) * n + j0 + c] : 0.0f;
+    {
+        // the tile's loads all in flight at once (this kernel is a step of the
+        // factorisation's serial chain)
+        constexpr int Q = kNB * kNB / 256;
+        float li[Q], bv[Q];
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const int idx = t + 256 * q, r = idx / kNB, c = idx % kNB;
+            li[q] = (r < nb && c < nb) ? Linv[idx] : 0.0f;
+            bv[q] = (r0 + r < rest && c < nb) ? A[(size_t)(j0 + nb + r0 + r) * n + j0 + c] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const int idx = t + 256 * q, r = idx / kNB, c = idx % kNB;
+            LI[r][c] = li[q];
+            B[r][c] = bv[q];
+        }
     }
     __syncthreads();
     const int rb = 4 * (t >> 4), cb = t & 15;   // rows rb..rb+3, columns cb + 16 j
