@@ -266,7 +266,20 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
         int grid_big = sms, grid_side = 0;
         bool conc = false;
         if (ng > 1 && a.side && a.lazy_ws && sms > 1) {
-            grid_big = (int)((double)sms * (double)g[big].nb / (double)total + 0.5);
+            // SMs in proportion to each side's work: tiles x the time of a
+            // tile at its K (lazy encoder, ms per tile-slot x 1000, measured on
+            // B200 at 20 tiles per SM: K = 2..7)
+            static const double kTileCost[8] = {0, 0, 593, 547, 522, 495, 523, 535};
+            double wtot = 0.0, wbig = 0.0;
+            for (int i = 0; i < ng; ++i) {
+                const double w = (double)g[i].nb * kTileCost[g[i].K];
+                wtot += w;
+                if (w > wbig) {
+                    wbig = w;
+                    big = i;
+                }
+            }
+            grid_big = (int)((double)sms * wbig / wtot + 0.5);
             grid_big = grid_big < 1 ? 1 : (grid_big > sms - 1 ? sms - 1 : grid_big);
             grid_side = sms - grid_big;
             conc = lazy_pipeline(g[big].K, g[big].nb, grid_big);
