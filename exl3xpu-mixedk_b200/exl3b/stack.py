@@ -254,12 +254,11 @@ def quantize_layer_split(layer: int, device, group=None, Ks: dict | None = None,
     """One layer of the stack with its output channels spread over the ranks
     of `group` (layer_ranges; a single process is a world of one).  Each rank
     factors the Hessian of every input group it touches once, quantizes its
-    channel ranges of each group in one sweep (exl3b.shard.
-    quantize_columns_fused: bit-identical to the same channels of the
-    unsplit tensors, self-checked), and the finished
-    trellises and scales are all-gathered (NCCL).  Rank 0 assembles each
-    tensor and writes its EXL3 files; returns its per-tensor stats there, []
-    on the other ranks."""
+    channel ranges of each group in one sweep (shard.quantize_columns_fused:
+    bit-identical to the same channels of the unsplit tensors, self-checked),
+    and the finished trellises and scales are all-gathered (NCCL).  Rank 0
+    assembles each tensor and writes its EXL3 files; returns its per-tensor
+    stats there, [] on the other ranks."""
     import torch
     import torch.distributed as dist
 
