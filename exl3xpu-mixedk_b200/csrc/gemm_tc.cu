@@ -300,13 +300,13 @@ feedback_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 // K rounded up to 32, zero padded), each value x (times `sign`) as
 // hi = tf32(x), lo = tf32(x - hi) -- the same split as split_row.  Then
 // gemm_tf32x3_kernel: persistent, warp-specialised 3xTF32 GEMM over pre-split
-// operands.  One CTA per SM walks the 128 x 128 tiles of C (row-major tile
+// operands.  One CTA per SM walks the 128 x BN tiles of C (row-major tile
 // order, CTA b takes tiles b, b + grid, ...):
-//   * warp 0 (one thread) streams 128 x 32 boxes of the four arrays with TMA
+//   * warp 0 (one thread) streams 128 x 32 / BN x 32 boxes of the four arrays with TMA
 //     (128-byte swizzle: the boxes land in the UMMA K-major canonical layout
 //     as they are) through a kStages ring of full / empty mbarriers;
 //   * warp 1 (one thread) issues the MMAs (lo.hi, hi.lo, hi.hi per 8-deep k
-//     step, as above) into one of two 128-column TMEM accumulators, tile by
+//     step, as above) into one of two BN-column TMEM accumulators, tile by
 //     tile in turn, and commits each stage back to the loader and each
 //     finished tile to the epilogue;
 //   * warps 2-5 (warp w reads TMEM lanes 32 (w mod 4) ..) run the epilogue,
@@ -317,11 +317,40 @@ feedback_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 // Every wait is bounded; on a time-out the CTA records the error, stops
 // issuing, waits (bounded) for its outstanding copies and MMAs, frees its
 // tensor memory and returns.
-constexpr int kStages = 3;
+// Tile width BN: 128 x 256 tiles (general updates) stream a quarter fewer
+// operand bytes per FLOP than 128 x 128 (the kernel is bound by the hi and lo
+// boxes it reads out of L2, about 10 TB/s at 128 x 128): two 96 KB stages and
+// two 256-column accumulators (all 512 TMEM columns).  128 x 128 tiles (three
+// 64 KB stages) stay for the lower-triangle updates, whose narrow trailing
+// blocks give too few wide tiles and whose wide tiles waste more work above
+// the diagonal.
 constexpr int kSplitK = 512;                        // K per pre-split piece
 constexpr int kOpBox = 128 * kTK * 4;               // one 128 x 32 tf32 tile: 16 KB
-constexpr int kStage2 = 4 * kOpBox;                 // Ah | Al | Bh | Bl
-constexpr int kGemm2Smem = kStages * kStage2 + 128 + 1024;   // ring | barriers | align
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int kStages = BN == 256 ? 2 : 3;
+    static constexpr int kBBox = BN * kTK * 4;                 // one BN x 32 tf32 box
+    static constexpr int kStage = 2 * kOpBox + 2 * kBBox;      // Ah | Al | Bh | Bl
+    static constexpr int kSmem = kStages * kStage + 128 + 1024;   // ring | barriers | align
+    // instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = BN
+    static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10)
+                                     | ((uint32_t)(BN >> 3) << 17)
+                                     | ((uint32_t)(kTM >> 4) << 24);
+    static_assert(kSmem <= 227 * 1024, "shared memory of one CTA");
+    static_assert(2 * BN <= 512, "two accumulators in the TMEM of one SM");
+};
+
+template <int BN>
+__device__ __forceinline__ void umma_tf32_n(uint32_t tmem_d, uint64_t da, uint64_t db,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(tmem_d), "l"(da), "l"(db), "r"(GemmCfg<BN>::kIdesc), "r"(accumulate)
+        : "memory");
+}
 
 __global__ void __launch_bounds__(256)
 tf32_split_kernel(const float* __restrict__ X, int ld, int K, int R, float sign,
@@ -347,14 +376,15 @@ tf32_split_kernel(const float* __restrict__ X, int ld, int K, int R, float sign,
 
 constexpr int kGemmThreads = 192;                   // loader, MMA, 4 epilogue warps
 
-// 128 x 128 tile t of the row-major tile grid (tn tiles per row); false when
+// 128 x BN tile t of the row-major tile grid (tn tiles per row); false when
 // `lower` skips it (entirely above the diagonal)
-__device__ __forceinline__ bool gemm_tile(int t, int tn, int lower, int& m0, int& n0) {
+__device__ __forceinline__ bool gemm_tile(int t, int tn, int bn, int lower, int& m0, int& n0) {
     m0 = (t / tn) * kTM;
-    n0 = (t % tn) * kTN;
+    n0 = (t % tn) * bn;
     return !(lower && n0 > m0 + kTM - 1);
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
                    const __grid_constant__ CUtensorMap tmAl,
@@ -362,6 +392,8 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
                    const __grid_constant__ CUtensorMap tmBl,
                    float* __restrict__ C, int ldc, int M, int N, int kp, float sa,
                    int lower, int* __restrict__ err) {
+    using Cfg = GemmCfg<BN>;
+    constexpr int kStages = Cfg::kStages, kStage2 = Cfg::kStage, kBBox = Cfg::kBBox;
     extern __shared__ __align__(1024) uint8_t gsm_raw[];
     uint8_t* gsm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + kStages * kStage2);
@@ -371,7 +403,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
     __shared__ int fail_s;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int tm = (M + kTM - 1) / kTM, tn = (N + kTN - 1) / kTN;
+    const int tm = (M + kTM - 1) / kTM, tn = (N + BN - 1) / BN;
     const int ntiles = tm * tn;
     const uint32_t full0 = smem_u32(&bars[0]);
     const uint32_t empty0 = smem_u32(&bars[kStages]);
@@ -390,7 +422,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_u32(tmem_slot)), "r"(2 * kTN) : "memory");
+                     :: "r"(smem_u32(tmem_slot)), "r"(2 * BN) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -405,7 +437,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
         bool ok = true;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
             int m0, n0;
-            if (!gemm_tile(tile, tn, lower, m0, n0)) continue;
+            if (!gemm_tile(tile, tn, BN, lower, m0, n0)) continue;
             for (int kc = 0; kc < nchunks; ++kc, ++it) {
                 const int s = it % kStages, r = it / kStages;
                 if (r > 0) ok = mbar_wait(empty0 + 8 * s, (r - 1) & 1);
@@ -417,7 +449,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
                 tma_load_2d(dst, &tmAh, kc * kTK, m0, bar);
                 tma_load_2d(dst + kOpBox, &tmAl, kc * kTK, m0, bar);
                 tma_load_2d(dst + 2 * kOpBox, &tmBh, kc * kTK, n0, bar);
-                tma_load_2d(dst + 3 * kOpBox, &tmBl, kc * kTK, n0, bar);
+                tma_load_2d(dst + 2 * kOpBox + kBBox, &tmBl, kc * kTK, n0, bar);
                 issued = it + 1;
             }
         }
@@ -433,26 +465,26 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
         bool ok = true;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
             int m0, n0;
-            if (!gemm_tile(tile, tn, lower, m0, n0)) continue;
+            if (!gemm_tile(tile, tn, BN, lower, m0, n0)) continue;
             const int a = lt & 1, u = lt >> 1;
             if (u > 0) ok = mbar_wait(aempty0 + 8 * a, (u - 1) & 1);
             if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t acc = tmem + (uint32_t)(a * kTN);
+            const uint32_t acc = tmem + (uint32_t)(a * BN);
             for (int kc = 0; kc < nchunks; ++kc, ++it) {
                 const int s = it % kStages, r = it / kStages;
                 ok = mbar_wait(full0 + 8 * s, r & 1);
                 if (!ok || *(volatile int*)&fail_s) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t aH = smem_u32(gsm + s * kStage2), aL = aH + kOpBox;
-                const uint32_t bH = aH + 2 * kOpBox, bL = aH + 3 * kOpBox;
+                const uint32_t bH = aH + 2 * kOpBox, bL = bH + kBBox;
 #pragma unroll
                 for (int kk = 0; kk < kTK / 8; ++kk) {
                     const uint32_t off = kk * 32;
-                    umma_tf32(acc, umma_desc_k_sw128(aL + off), umma_desc_k_sw128(bH + off),
-                              (kc > 0 || kk > 0) ? 1u : 0u);
-                    umma_tf32(acc, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bL + off), 1u);
-                    umma_tf32(acc, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bH + off), 1u);
+                    umma_tf32_n<BN>(acc, umma_desc_k_sw128(aL + off), umma_desc_k_sw128(bH + off),
+                                (kc > 0 || kk > 0) ? 1u : 0u);
+                    umma_tf32_n<BN>(acc, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bL + off), 1u);
+                    umma_tf32_n<BN>(acc, umma_desc_k_sw128(aH + off), umma_desc_k_sw128(bH + off), 1u);
                 }
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                              :: "r"(empty0 + 8 * s) : "memory");
@@ -473,7 +505,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
         int lt = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             int m0, n0;
-            if (!gemm_tile(tile, tn, lower, m0, n0)) continue;
+            if (!gemm_tile(tile, tn, BN, lower, m0, n0)) continue;
             const int a = lt & 1, u = lt >> 1;
             bool ok = mbar_wait(afull0 + 8 * a, u & 1);
             // one decision per warp: the TMEM loads below are warp-collective
@@ -485,9 +517,9 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int row = m0 + 32 * q + lane;
 #pragma unroll 1
-            for (int cc = 0; cc < kTN / 32; ++cc) {
+            for (int cc = 0; cc < BN / 32; ++cc) {
                 uint32_t r[32];
-                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * kTN + 32 * cc);
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * BN + 32 * cc);
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
                     "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -501,7 +533,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
                       "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                     : "r"(taddr));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (cc == kTN / 32 - 1) {
+                if (cc == BN / 32 - 1) {
                     // the accumulator is read out: hand it back to the MMA issuer
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];"
@@ -539,7 +571,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh,
     __syncthreads();
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
-                     :: "r"(tmem), "r"(2 * kTN) : "memory");
+                     :: "r"(tmem), "r"(2 * BN) : "memory");
 }
 
 // ---------------------------------------------------------------- host side
@@ -586,10 +618,11 @@ static int encode_operand(CUtensorMap* map, const float* base, int inner, int ou
     return RC_OK;
 }
 
-static int encode_split(CUtensorMap* map, const float* base, int kp, int rows) {
+static int encode_split(CUtensorMap* map, const float* base, int kp, int rows,
+                        int box_rows = 128) {
     cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)kp * 4};
-    cuuint32_t box[2] = {(cuuint32_t)kTK, 128};
+    cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     EncodeTiledFn enc = encode_fn();
     if (!enc) {
@@ -624,17 +657,18 @@ int gemm_split(const float* X, int ld, int K, int R, float* hi, float* lo, int k
     return check_cuda(cudaGetLastError(), "tf32_split launch") ? RC_DEVICE_ERROR : RC_OK;
 }
 
-int gemm_presplit_run(int M, int N, int kp, const float* Ah, const float* Al, const float* Bh,
-                      const float* Bl, float* C, int ldc, float sa, int lower, int* err,
-                      cudaStream_t stream) {
-    if (M <= 0 || N <= 0) return RC_OK;
+template <int BN>
+static int presplit_launch(int M, int N, int kp, const float* Ah, const float* Al,
+                           const float* Bh, const float* Bl, float* C, int ldc, float sa,
+                           int lower, int* err, cudaStream_t stream) {
+    using Cfg = GemmCfg<BN>;
     static bool attr[kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev]) {
-        if (check_cuda(cudaFuncSetAttribute(gemm_tf32x3_kernel,
+        if (check_cuda(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kGemm2Smem),
+                                            Cfg::kSmem),
                        "cudaFuncSetAttribute(gemm_tf32x3)"))
             return RC_DEVICE_ERROR;
         attr[dev] = true;
@@ -642,16 +676,24 @@ int gemm_presplit_run(int M, int N, int kp, const float* Ah, const float* Al, co
     CUtensorMap tAh, tAl, tBh, tBl;
     int rc = encode_split(&tAh, Ah, kp, M);
     if (!rc) rc = encode_split(&tAl, Al, kp, M);
-    if (!rc) rc = encode_split(&tBh, Bh, kp, N);
-    if (!rc) rc = encode_split(&tBl, Bl, kp, N);
+    if (!rc) rc = encode_split(&tBh, Bh, kp, N, BN);
+    if (!rc) rc = encode_split(&tBl, Bl, kp, N, BN);
     if (rc) return rc;
-    const int tiles = ((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
+    const int tiles = ((N + BN - 1) / BN) * ((M + kTM - 1) / kTM);
     const int sms = device_sms();
     const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);     // persistent CTAs
-    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemm2Smem, stream>>>(tAh, tAl, tBh, tBl, C, ldc,
-                                                                  M, N, kp, sa, lower, err);
+    gemm_tf32x3_kernel<BN><<<grid, kGemmThreads, Cfg::kSmem, stream>>>(
+        tAh, tAl, tBh, tBl, C, ldc, M, N, kp, sa, lower, err);
     note_launch();
     return check_cuda(cudaGetLastError(), "gemm_tf32x3 launch") ? RC_DEVICE_ERROR : RC_OK;
+}
+
+int gemm_presplit_run(int M, int N, int kp, const float* Ah, const float* Al, const float* Bh,
+                      const float* Bl, float* C, int ldc, float sa, int lower, int* err,
+                      cudaStream_t stream) {
+    if (M <= 0 || N <= 0) return RC_OK;
+    return lower ? presplit_launch<128>(M, N, kp, Ah, Al, Bh, Bl, C, ldc, sa, lower, err, stream)
+                 : presplit_launch<256>(M, N, kp, Ah, Al, Bh, Bl, C, ldc, sa, lower, err, stream);
 }
 
 // C[M][N] += sa * A_T^T . B on tcgen05 (A_T [K][M], B [K][N], both row-major
