@@ -527,7 +527,8 @@ def main():
     tpw = TRAFFIC_BYTES_PER_WEIGHT_K4 if shape.get("K") == 4 else None
     roofline = {
         "kernel": "LDLQ tile kernel (fused feedback + tail-biting Viterbi + write-back; "
-                  "ldlq_lazy_kernel for launches of >= 2 tiles per SM)",
+                  "ldlq_lazy_kernel for launches of >= 2 tiles per SM; ldlq_solo_kernel where the "
+                  "column tiles do not fill the SMs)",
         "bound": "fp32", "achieved": achieved, "peak": peak_ops, "unit": "Gop/s",
         "frac": achieved / peak_ops,
         "peak_source": f"{sms} SMs x 128 fp32 lanes x {mhz:.0f} MHz (sm_max_mhz of "

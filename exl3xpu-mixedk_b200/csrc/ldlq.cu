@@ -13,8 +13,9 @@
 // launch buffers of max(buf_cols, 512) rows.  One tile-kernel launch per
 // buffer covers all its k-blocks x
 // column tiles.  Launches with at least two tiles per SM use the persistent
-// lazy-argmin kernel (ldlq_lazy.cu); the others, one CTA per tile
-// with the traced encoder, below.  Each CTA takes a ticket in dependency order (k-block
+// lazy-argmin kernel (ldlq_lazy.cu), launches whose column tiles do not fill
+// the SMs its one-tile-per-CTA variant (same file); the others, one CTA per
+// tile with the traced encoder, below.  Each CTA takes a ticket in dependency order (k-block
 // descending, column ascending) and, when it needs the block below it in the
 // same column (intra-buffer feedback), waits on that column's progress
 // counter.  The producer of that block took an earlier ticket, so it is
@@ -29,6 +30,7 @@
 //   states = tail-biting encode(x)                         (:687-731)
 //   hatW[perm[t]] = lut[states[t]], E = Wq - hatW          (:736-741)
 //   trellis = pack(states)                                 (:846, :360-378)
+#include <stdlib.h>
 #include <string.h>
 
 #include "exl3b_internal.h"
@@ -36,6 +38,19 @@
 #include "viterbi.cuh"
 
 namespace exl3b {
+
+// Column tiles up to which a launch of `grid` CTAs at K runs one tile per CTA
+// at a time (ldlq_solo_kernel): `grid`, where each column's chain of k-blocks
+// keeps at most one CTA busy -- except at K = 6, where the one-tile kernel
+// measured 5.5% slower (0.694 against 0.658 ms per k-block at 32 column
+// tiles; K = 2, 3, 4, 5, 7: 9.5, 8, 7.7, 6.4, 8% faster).  EXL3B_SOLO_COLS (a
+// column count, 0 = never) replaces it for every K; the tests use it to run
+// both kernels on the same shapes.
+static int solo_max_cols(int grid, int K) {
+    const char* e = getenv("EXL3B_SOLO_COLS");
+    if (e != nullptr && *e != 0) return atoi(e);
+    return K == 6 ? 0 : grid;
+}
 
 // sched (shared): [0] k-block i, [1] column tile c, [2] backpointer slot,
 // [3] ok, [4] column segment.  Re-read where needed instead of being kept
@@ -307,9 +322,13 @@ int ldlq_sweep(const SweepArgs& a, cudaStream_t stream) {
             p.ntiles = (int)G.nb;
             const int grid = conc ? (on_side ? grid_side : grid_big) : sms;
             if (!conc) prof_begin_launch(s, PROF_TILE, (double)G.nb * 256.0);
-            // at least two tiles per SM: persistent CTAs, lazy argmin
+            // at least two tiles per SM: persistent CTAs, lazy argmin; one tile
+            // per CTA at a time when the column tiles do not fill the CTAs
             const bool lazy = a.lazy_ws != nullptr && lazy_pipeline(G.K, G.nb, grid);
-            const int rc = lazy ? launch_lazy_tile(G.K, p, (unsigned)grid, s)
+            const bool solo = a.lazy_ws != nullptr && G.K >= kLazyMinK &&
+                              G.ls_pre[G.nls] <= solo_max_cols(grid, G.K);
+            const int rc = solo ? launch_solo_tile(G.K, p, (unsigned)grid, s)
+                         : lazy ? launch_lazy_tile(G.K, p, (unsigned)grid, s)
                                 : launch_tile(G.K, p, (unsigned)G.nb, s);
             if (!conc) prof_end_launch(s);
             if (rc) return rc;

@@ -1,5 +1,7 @@
-// ldlq_lazy.cu -- the LDLQ sweep's tile kernel with the lazy-argmin encoder
-// (vit_lazy.cuh), used for launches with at least two tiles per SM.
+// ldlq_lazy.cu -- the LDLQ sweep's tile kernels with the lazy-argmin encoder
+// (vit_lazy.cuh): the two-tile pipeline for launches with at least two tiles
+// per SM, and a one-tile-per-CTA variant (ldlq_solo_kernel, below) for
+// launches whose column tiles do not fill the SMs.
 //
 // Persistent CTAs (one per SM, 16 forward warps + the traceback warp) take
 // tiles by ticket in the same dependency order as the one-tile-per-CTA kernel
@@ -244,6 +246,97 @@ ldlq_lazy_kernel(const __grid_constant__ LdlqTileParams p) {
         tb_job_drain<K>(smem, p.lut32, t);
         lazy_release<K>(p, smem, sc, 1, t);
     }
+}
+
+// One tile at a time per CTA, for launches whose column tiles do not fill the
+// CTAs: there every CTA of the two-tile pipeline holds a lone tile (its next
+// tile waits on the one it holds) and runs it through the "A alone" sequence
+// above, with the traceback warp's register cap on the forward warps.  Here
+// the CTA has the 16 forward warps only -- 128 registers per thread instead
+// of 96 -- and warp 0 runs each traceback between the passes while the
+// others wait: F1, T1, F2, T2, write-back, next ticket.  The same passes and
+// jobs as the pipeline, so the same states.  A CTA that waits for a
+// dependency holds no tile, so the ticket argument of the pipeline holds.
+template <int K>
+__global__ void __launch_bounds__(kVT, 1)
+ldlq_solo_kernel(const __grid_constant__ LdlqTileParams p) {
+    extern __shared__ __align__(16) char smem[];
+    using SM = LazySmem<K>;
+    using TS = LazyTileSmem<K>;
+    using L = Lazy<K>;
+    const int t = threadIdx.x;
+    __half2 f2[64];
+    vit_load_f2tab(f2, p.f2tab[K], t);
+    float* xs = reinterpret_cast<float*>(smem + SM::OFF_X);
+    int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST);
+    float* wx = reinterpret_cast<float*>(smem + TS::OFF_WX);
+    float* gst = reinterpret_cast<float*>(smem + TS::OFF_GATHER);
+    volatile TbJob* jb = reinterpret_cast<volatile TbJob*>(smem + SM::OFF_JOB);
+    volatile LazySched* sc = reinterpret_cast<volatile LazySched*>(smem + TS::OFF_SCHED);
+    float* reg0 = p.lazy_ws + (size_t)(2 * blockIdx.x) * (L::REGION / 4);
+    const int pivot = p.pivot;
+    const int n1 = (p.margin > 0 && pivot + p.margin < kSteps) ? pivot + p.margin : kSteps;
+    if (t == 0) {
+        jb->active = 0;
+        sc->ok = 1;
+    }
+    __syncthreads();
+    for (;;) {
+        if (t == 0) {
+            lazy_fetch(p, sc, 0);
+            if (sc->got) lazy_wait_dep(p, sc, 0);
+        }
+        __syncthreads();
+        if (!sc->got || !sc->ok) break;
+        tile_feedback_gather(p, sc->i[0], sc->c[0], xs, wx, gst, t, kVT);
+        const int f1 = lazy_pass<K>(f2, smem, 0, pivot, n1, -1, pivot, reg0, nullptr,
+                                    p.lut32, t);
+        if (t == 0) tb_job_start<K>(smem, reg0, 0, 0, pivot, -1, pivot, n1 - 1, f1);
+        __syncthreads();
+        if (t < 32) tb_job_run<K>(smem, p.lut32, t);
+        __syncthreads();
+        const int sp = jb->result;
+        __syncthreads();
+        const int f2s = lazy_pass<K>(f2, smem, 0, 0, kSteps, sp >> K, 0, reg0,
+                                     &st[kSteps - 1], p.lut32, t);
+        if (t == 0) tb_job_start<K>(smem, reg0, 0, 1, 0, sp >> K, 0, kSteps - 1, f2s);
+        __syncthreads();
+        if (t < 32) tb_job_run<K>(smem, p.lut32, t);
+        __syncthreads();
+        lazy_release<K>(p, smem, sc, 0, t);
+        __syncthreads();
+    }
+}
+
+template <int K>
+static int launch_solo_tile_k(const LdlqTileParams& p, unsigned grid, cudaStream_t stream) {
+    static bool attr[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev]) {
+        if (check_cuda(cudaFuncSetAttribute(ldlq_solo_kernel<K>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            LazyTileSmem<K>::BYTES),
+                       "cudaFuncSetAttribute(ldlq_solo)"))
+            return RC_DEVICE_ERROR;
+        attr[dev] = true;
+    }
+    ldlq_solo_kernel<K><<<grid, kVT, LazyTileSmem<K>::BYTES, stream>>>(p);
+    note_launch();
+    return check_cuda(cudaGetLastError(), "ldlq_solo_kernel launch") ? RC_DEVICE_ERROR : RC_OK;
+}
+
+int launch_solo_tile(int K, const LdlqTileParams& p, unsigned grid, cudaStream_t stream) {
+    switch (K) {
+        case 2: return launch_solo_tile_k<2>(p, grid, stream);
+        case 3: return launch_solo_tile_k<3>(p, grid, stream);
+        case 4: return launch_solo_tile_k<4>(p, grid, stream);
+        case 5: return launch_solo_tile_k<5>(p, grid, stream);
+        case 6: return launch_solo_tile_k<6>(p, grid, stream);
+        case 7: return launch_solo_tile_k<7>(p, grid, stream);
+    }
+    set_error("solo tile kernel: K=%d outside 2..7", K);
+    return RC_BAD_K;
 }
 
 template <int K>

@@ -185,5 +185,7 @@ __device__ __forceinline__ void tile_writeback(const LdlqTileParams& p, int i, i
 
 // ldlq_lazy.cu: persistent lazy-argmin tile kernel for K = 2..7, `grid` CTAs
 int launch_lazy_tile(int K, const LdlqTileParams& p, unsigned grid, cudaStream_t stream);
+// ldlq_lazy.cu: the same encoder one tile at a time per CTA (narrow launches)
+int launch_solo_tile(int K, const LdlqTileParams& p, unsigned grid, cudaStream_t stream);
 
 }  // namespace exl3b

@@ -375,12 +375,21 @@ def test_stored_fields_dequantise_to_w_hat(xq, tmp_path):
                                      # pending tiles are often a new tile's dependency
     (4864, 16, 4, 4864, 128, 0),     # one column: every B depends on its A
 ])
-def test_lazy_sweep_dual_check(xq, oracle, mul1_lut, k, n, K, buf_cols, pivot, margin):
+@pytest.mark.parametrize("solo_cols", ("", "0"))
+def test_lazy_sweep_dual_check(xq, oracle, mul1_lut, k, n, K, buf_cols, pivot, margin,
+                               solo_cols, monkeypatch):
     """Buffer launches of >= 2 tiles per SM run the persistent
-    lazy-argmin tile kernel: every k-block's encoder targets, re-encoded by the
-    CPU oracle, give the sweep's states (the reference's per-launch dual
-    check), and the trellis decodes to hatW."""
+    lazy-argmin tile kernel, and launches whose column tiles do not fill the
+    SMs the one-tile-per-CTA variant (EXL3B_SOLO_COLS unset; "0" forces the
+    two-tile pipeline, or the traced kernel for launches of < 2 tiles per SM):
+    every k-block's encoder targets, re-encoded by the CPU oracle, give the
+    sweep's states (the reference's per-launch dual check), and the trellis
+    decodes to hatW."""
     from exl3b import api
+    if solo_cols:
+        monkeypatch.setenv("EXL3B_SOLO_COLS", solo_cols)
+    else:
+        monkeypatch.delenv("EXL3B_SOLO_COLS", raising=False)
     W, H = _ldlq_problem(k, 16, 50 + K)
     dev = torch.device("cuda", 0)
     Lfac = api._damped_lfac(H, xq.sign_vec(k, 9).half(), 0.01, dev)
