@@ -458,7 +458,8 @@ int exl3b_ldlq_sweep(const float* dWq, const float* dLfac, int k, int n, int nse
                   "%d %d %d %d %d %d %d %d",
                   err[0] == 1 ? "no free backpointer slot" :
                   err[0] == 2 ? "dependency wait timed out" :
-                  err[0] == 4 ? "feedback GEMM barrier timed out" : "aborted", err[1], err[2],
+                  err[0] == 4 ? "feedback GEMM barrier timed out" :
+                  err[0] == 5 ? "traceback row staging wait timed out" : "aborted", err[1], err[2],
                   err[3], err[4], err[13], a.nslots, err[5], err[6], err[7], err[8], err[9],
                   err[10], err[11], err[12]);
         return RC_DEVICE_ERROR;

@@ -248,6 +248,144 @@ ldlq_lazy_kernel(const __grid_constant__ LdlqTileParams p) {
     }
 }
 
+// ---- tracebacks of the one-tile kernel from staged rows (K = 4)
+// No pass uses the best-array ring while a traceback runs.  Thread 32 streams
+// the rows the traceback will read, in its order, into the ring with bulk
+// copies (global -> shared, no multicast; one "full" and one "empty" mbarrier
+// per slot), up to Lazy<K>::RING rows ahead.  Warp 0 reads each row's
+// candidates from its slot and the decode values from an fp16 copy of the
+// code table in shared memory (exact: the decode values are fp16 values).  A
+// row then costs shared-memory loads and two warp minima instead of a round
+// trip to L2 for its 2^K candidates and decode values.  Same candidates, same
+// operations, same first-index minimum as tb_job_run.  Measured per k-block
+// at 32 column tiles: K = 4 0.664 -> 0.593 ms (128 column tiles: 0.756 ->
+// 0.641); K = 3 0.713 -> 0.788 (its 32 KB rows leave two slots, and the
+// copies cannot keep ahead), so K = 3 keeps tb_job_run.
+#ifndef EXL3B_SOLO_STAGE
+#define EXL3B_SOLO_STAGE 1
+#endif
+
+template <int K>
+struct SoloSmem {
+    static constexpr bool STAGE = K == 4 && EXL3B_SOLO_STAGE;
+    static constexpr int NR = Lazy<K>::RING;                  // staging slots
+    static constexpr int OFF_LUT = (LazyTileSmem<K>::BYTES + 127) / 128 * 128;
+    static constexpr int OFF_BAR = OFF_LUT + (STAGE ? 65536 * 2 : 0);
+    static constexpr int BYTES = OFF_BAR + (STAGE ? 2 * NR * 8 : 0);
+    static_assert(BYTES <= 227 * 1024, "shared memory of one CTA");
+    static_assert(NR * Lazy<K>::ROW_BYTES <= LazySmem<K>::OFF_X, "slots inside the ring");
+};
+
+__device__ __forceinline__ bool solo_mbar_wait(uint32_t bar, uint32_t parity, long long limit) {
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+        if (ok) return true;
+        if (clock64() - t0 > limit) return false;
+    }
+}
+
+// thread 32: stage rows r0 - 1 .. max(stop, 1) (running row count g0 at the
+// first) into the ring; use u of slot g % NR waits for the release of use
+// u - 1.  Returns false if a wait timed out; `issued` counts the copies sent.
+template <int K>
+__device__ __forceinline__ bool solo_stage_rows(const float* rows, int r0, int stop, char* smem,
+                                                uint32_t full0, uint32_t empty0, int g0,
+                                                long long limit, int& issued) {
+    using G = Geo<K>;
+    using L = Lazy<K>;
+    constexpr int NR = SoloSmem<K>::NR;
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(smem + LazySmem<K>::OFF_RING);
+    const int n = r0 - max(stop, 1);
+    for (int i = 0; i < n; ++i) {
+        const int q = r0 - 1 - i, gr = g0 + i, slot = gr % NR;
+        if (gr >= NR && !solo_mbar_wait(empty0 + 8 * slot, ((gr / NR) - 1) & 1, limit))
+            return false;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                     :: "r"(full0 + 8 * slot), "r"(L::ROW_BYTES) : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+            :: "r"(ring + (uint32_t)(slot * L::ROW_BYTES)), "l"(rows + (size_t)q * G::SPRE),
+               "r"(L::ROW_BYTES), "r"(full0 + 8 * slot)
+            : "memory");
+        ++issued;
+    }
+    return true;
+}
+
+// warp 0: the armed traceback job over the staged rows (running row count g0
+// at row r0 - 1).  Returns false if a wait timed out.
+template <int K>
+__device__ __forceinline__ bool solo_traceback(char* smem, const __half* __restrict__ lut16,
+                                               int lane, uint32_t full0, uint32_t empty0,
+                                               int g0, long long limit) {
+    using G = Geo<K>;
+    using SM = LazySmem<K>;
+    using L = Lazy<K>;
+    constexpr int NR = SoloSmem<K>::NR;
+    static_assert(G::NC <= 32 && !L::HALF && L::BULK, "one candidate per lane, full rows");
+    volatile TbJob* jb = reinterpret_cast<volatile TbJob*>(smem + SM::OFF_JOB);
+    const bool want = jb->want_states != 0;
+    const int slot0 = jb->slot, rol = jb->rol, overlap = jb->overlap, stop = jb->stop;
+    const int r0 = jb->r;
+    int s = jb->s;
+    __syncwarp();
+    const float* xs = reinterpret_cast<const float*>(smem + SM::OFF_X) + 256 * slot0;
+    int32_t* st = reinterpret_cast<int32_t*>(smem + SM::OFF_ST) + 256 * slot0;
+    const float* ring = reinterpret_cast<const float*>(smem + SM::OFF_RING);
+    const float INF = __int_as_float(0x7f800000);
+    bool ok = true;
+    int r = r0;
+    for (; r > stop; --r) {
+        const int j = (s & 0xFFFF) >> K;      // states are 16-bit
+        const int m = j >> K;
+        const int q = r - 1;
+        const float x = xs[(q - rol) & 255];
+        int slot = 0;
+        if (q >= 1) {
+            const int gr = g0 + (r0 - 1 - q);
+            slot = gr % NR;
+            ok = __all_sync(0xffffffffu, solo_mbar_wait(full0 + 8 * slot, (gr / NR) & 1, limit));
+            if (!ok) break;
+        }
+        uint32_t kc = 0xFFFFFFFFu, kw = 0xFFFFFFFFu;
+        if (lane < G::NC) {
+            const int idx = m + lane * G::P;
+            const float b = (q == 0) ? ((overlap < 0 || idx == overlap) ? 0.0f : INF)
+                                     : ring[slot * (L::ROW_BYTES / 4) + G::baddr(idx)];
+            const float d = __fsub_rn(__half2float(lut16[j + (lane << (16 - K))]), x);
+            kc = __float_as_uint(__fadd_rn(__fmul_rn(d, d), b));
+            kw = (uint32_t)lane;
+        }
+        const uint32_t cmin = __reduce_min_sync(0xffffffffu, kc);
+        const uint32_t wmin = __reduce_min_sync(0xffffffffu, kc == cmin ? kw : 0xFFFFFFFFu);
+        if (q >= 1) {
+            // this lane's reads of the slot precede the next copy into it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];"
+                             :: "r"(empty0 + 8 * slot) : "memory");
+        }
+        s = j + ((int)wmin << (16 - K));
+        if (want && lane == 0) st[q] = s;
+    }
+    __syncwarp();
+    if (lane == 0) {
+        jb->r = r;
+        jb->s = s;
+        jb->active = 0;
+        jb->result = s;
+    }
+    __syncwarp();
+    return ok;
+}
+
 // One tile at a time per CTA, for launches whose column tiles do not fill the
 // CTAs: there every CTA of the two-tile pipeline holds a lone tile (its next
 // tile waits on the one it holds) and runs it through the "A alone" sequence
@@ -276,11 +414,54 @@ ldlq_solo_kernel(const __grid_constant__ LdlqTileParams p) {
     float* reg0 = p.lazy_ws + (size_t)(2 * blockIdx.x) * (L::REGION / 4);
     const int pivot = p.pivot;
     const int n1 = (p.margin > 0 && pivot + p.margin < kSteps) ? pivot + p.margin : kSteps;
+    using SS = SoloSmem<K>;
+    __half* lut16 = reinterpret_cast<__half*>(smem + SS::OFF_LUT);
+    const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(smem + SS::OFF_BAR);
+    const uint32_t empty0 = full0 + 8 * SS::NR;
+    int g = 0;                  // rows staged so far (every thread keeps the count)
     if (t == 0) {
         jb->active = 0;
         sc->ok = 1;
+        if (SS::STAGE) {
+            for (int i = 0; i < 2 * SS::NR; ++i)
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(full0 + 8 * i)
+                             : "memory");
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
     }
+    if (SS::STAGE)
+        for (int i = t; i < 65536; i += kVT) lut16[i] = __float2half_rn(p.lut32[i]);
     __syncthreads();
+    // one traceback job (armed by thread 0 before the call's barrier): warp 0
+    // over staged rows with thread 32 staging them, or warp 0 alone
+    auto traceback = [&](bool& fail) {
+        if constexpr (SS::STAGE) {
+            const int r0 = jb->r, stop = jb->stop;
+            const float* rows = jb->rows;
+            int issued = 0;
+            bool ok = true;
+            if (t < 32)
+                ok = solo_traceback<K>(smem, lut16, t, full0, empty0, g, p.wait_cycles);
+            else if (t == 32)
+                ok = solo_stage_rows<K>(rows, r0, stop, smem, full0, empty0, g, p.wait_cycles,
+                                        issued);
+            fail = __syncthreads_or(!ok) != 0;
+            if (fail && t == 32) {
+                // the copies still in flight land before the CTA leaves
+                for (int i = issued > SS::NR ? issued - SS::NR : 0; i < issued; ++i)
+                    solo_mbar_wait(full0 + 8 * ((g + i) % SS::NR), ((g + i) / SS::NR) & 1,
+                                   p.wait_cycles);
+                if (atomicCAS(p.err, 0, 5) == 0) {
+                    p.err[1] = -1; p.err[2] = sc->i[0]; p.err[3] = sc->c[0]; p.err[4] = r0;
+                }
+            }
+            g += max(0, r0 - max(stop, 1));
+        } else {
+            if (t < 32) tb_job_run<K>(smem, p.lut32, t);
+            fail = false;
+        }
+        __syncthreads();
+    };
     for (;;) {
         if (t == 0) {
             lazy_fetch(p, sc, 0);
@@ -289,20 +470,24 @@ ldlq_solo_kernel(const __grid_constant__ LdlqTileParams p) {
         __syncthreads();
         if (!sc->got || !sc->ok) break;
         tile_feedback_gather(p, sc->i[0], sc->c[0], xs, wx, gst, t, kVT);
+        bool fail = false;
         const int f1 = lazy_pass<K>(f2, smem, 0, pivot, n1, -1, pivot, reg0, nullptr,
                                     p.lut32, t);
+        // the pass's generic writes to the ring precede the staging copies
+        if (SS::STAGE) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (t == 0) tb_job_start<K>(smem, reg0, 0, 0, pivot, -1, pivot, n1 - 1, f1);
         __syncthreads();
-        if (t < 32) tb_job_run<K>(smem, p.lut32, t);
-        __syncthreads();
+        traceback(fail);
+        if (fail) break;
         const int sp = jb->result;
         __syncthreads();
         const int f2s = lazy_pass<K>(f2, smem, 0, 0, kSteps, sp >> K, 0, reg0,
                                      &st[kSteps - 1], p.lut32, t);
+        if (SS::STAGE) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (t == 0) tb_job_start<K>(smem, reg0, 0, 1, 0, sp >> K, 0, kSteps - 1, f2s);
         __syncthreads();
-        if (t < 32) tb_job_run<K>(smem, p.lut32, t);
-        __syncthreads();
+        traceback(fail);
+        if (fail) break;
         lazy_release<K>(p, smem, sc, 0, t);
         __syncthreads();
     }
@@ -316,12 +501,12 @@ static int launch_solo_tile_k(const LdlqTileParams& p, unsigned grid, cudaStream
     if (!attr[dev]) {
         if (check_cuda(cudaFuncSetAttribute(ldlq_solo_kernel<K>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            LazyTileSmem<K>::BYTES),
+                                            SoloSmem<K>::BYTES),
                        "cudaFuncSetAttribute(ldlq_solo)"))
             return RC_DEVICE_ERROR;
         attr[dev] = true;
     }
-    ldlq_solo_kernel<K><<<grid, kVT, LazyTileSmem<K>::BYTES, stream>>>(p);
+    ldlq_solo_kernel<K><<<grid, kVT, SoloSmem<K>::BYTES, stream>>>(p);
     note_launch();
     return check_cuda(cudaGetLastError(), "ldlq_solo_kernel launch") ? RC_DEVICE_ERROR : RC_OK;
 }

@@ -166,12 +166,12 @@ ALIGN = 128
 # between candidate cuts.  A group's sweep over `cols` column tiles and tk
 # k-blocks takes about max(tk x CHAIN_MS, tk x cols / TILES_PER_MS): a column's
 # k-blocks are sequential, and a k-block of a narrow sweep (tiles alone on
-# their SMs, the one-tile-per-CTA kernel) takes ~0.65 ms (B200, in = 5120, 32
-# column tiles: K = 4 0.663, K = 5 0.603, K = 6 0.658, K = 7 0.642 ms per
-# k-block; K = 4 at 128 column tiles 0.758), while a full-width sweep retires
+# their SMs, the one-tile-per-CTA kernel) takes ~0.6 ms (B200, in = 5120, 32
+# column tiles: K = 4 0.593, K = 5 0.603, K = 6 0.658, K = 7 0.642 ms per
+# k-block; K = 4 at 128 column tiles 0.641), while a full-width sweep retires
 # ~278 tiles per ms on 148 SMs (config 2: 102400 tiles in 368 ms).  Plus the
 # group's Hessian synthesis and block LDL (~31 ms at in = 17408, ~7 ms below).
-CHAIN_MS = 0.65
+CHAIN_MS = 0.6
 TILES_PER_MS = 278.0
 
 
