@@ -251,10 +251,11 @@ ldlq_lazy_kernel(const __grid_constant__ LdlqTileParams p) {
 // ---- tracebacks of the one-tile kernel from staged rows (K = 4)
 // No pass uses the best-array ring while a traceback runs.  Thread 32 streams
 // the rows the traceback will read, in its order, into the ring with bulk
-// copies (global -> shared, no multicast; one "full" and one "empty" mbarrier
-// per slot), up to Lazy<K>::RING rows ahead.  Warp 0 reads each row's
-// candidates from its slot and the decode values from an fp16 copy of the
-// code table in shared memory (exact: the decode values are fp16 values).  A
+// copies (this GPU's global memory -> this CTA's shared memory; one "full"
+// and one "empty" mbarrier per slot), up to Lazy<K>::RING rows ahead.  Warp 0
+// reads each row's candidates from its slot and the decode values from an
+// fp16 copy of the code table in shared memory (exact: the decode values are
+// fp16 values).  A
 // row then costs shared-memory loads and two warp minima instead of a round
 // trip to L2 for its 2^K candidates and decode values.  Same candidates, same
 // operations, same first-index minimum as tb_job_run.  Measured per k-block
